@@ -324,16 +324,35 @@ def gen_recovery(retree, recovery, trees):
             post = logits.argmax(-1)
             # bias some steps towards children so exact accepts and rescues both occur
             path = synthetic.accepted_path(int(rng.integers(1 << 30)), case["parents"])
-            for a, b in zip(path[:-1], path[1:]):
-                if rng.random() < 0.6:
-                    logits[a, case["tokens"][b - 1]] += 8.0
+            stop_bias = int(rng.integers(0, len(path)))
+            for a, b in list(zip(path[:-1], path[1:]))[:stop_bias]:
+                logits[a, case["tokens"][b - 1]] += 8.0
             post = logits.argmax(-1)
             mem = recovery.RecoveryMemory(freq_threshold=int(rng.integers(1, 4)))
             prior = []
+            tree_toks = np.asarray(case["tokens"])
             for _ in range(int(rng.integers(40, 120))):
-                d, t, c = int(rng.integers(vocab)), int(rng.integers(vocab)), int(rng.integers(1, 4))
+                # mostly (tree token, target argmax) pairs, so that rescues happen
+                if rng.random() < 0.7:
+                    d, t = int(rng.choice(tree_toks)), int(rng.choice(post))
+                else:
+                    d, t = int(rng.integers(vocab)), int(rng.integers(vocab))
+                c = int(rng.integers(1, 4))
                 mem.record_prior(d, t, count=c)
                 prior.append((d, t, c))
+            # seed the prior with the pairs met at the exact walk's stopping point
+            # (the children the target ranks highest), so that rescues happen
+            cur, nxt0 = 0, int(post[0])
+            while nxt0 in maps[cur]:
+                cur = maps[cur][nxt0]
+                nxt0 = int(post[cur])
+            kids = list(maps[cur].keys())
+            kids.sort(key=lambda tk: -float(logits[cur, tk]))
+            for tk in kids[:3]:
+                if rng.random() < 0.7:
+                    c = int(rng.integers(1, 5))
+                    mem.record_prior(tk, nxt0, count=c)
+                    prior.append((tk, nxt0, c))
             stop = sorted({int(x) for x in rng.choice(vocab, size=2, replace=False)}) if trial else None
             acc, nxt, rescued = retree.follow_verified_tree_with_recovery(
                 maps, torch.from_numpy(post)[None], torch.from_numpy(logits)[None], mem,
