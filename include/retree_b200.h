@@ -1,0 +1,219 @@
+/*
+ * retree_b200 — C ABI of the B200 (sm_100a) kernels behind ReTree's
+ * tree-verification path.
+ *
+ * Conventions (every entry point):
+ *   - Plain device pointers, sizes and strides; no framework types.  Strides
+ *     are in BYTES unless a name says otherwise.
+ *   - Work is enqueued on `stream` (a cudaStream_t; NULL = legacy default
+ *     stream).  Nothing here allocates device memory: scratch ("workspace") is
+ *     passed in by the caller, sized by the matching *_workspace_size call.
+ *   - The return value is an RT_* code checked on the host before launch
+ *     (arguments, shapes, launch errors).  Kernels report data-dependent
+ *     errors (an index out of range, a wait that ran out) by writing an
+ *     RT_DEV_* code into the optional device word `status` (first error wins;
+ *     the caller zeroes it).
+ *   - Results are bit-for-bit deterministic run to run.
+ *
+ * Each declaration names the reference interface (Adamlong3/ReTree, or the
+ * transformers 5.5.0 code the reference calls) that it replaces.
+ */
+#ifndef RETREE_B200_H
+#define RETREE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* rt_stream_t;
+
+/* Host-side return codes. */
+#define RT_OK 0
+#define RT_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, misaligned stride */
+#define RT_ERR_UNSUPPORTED 2      /* valid but outside what the kernels implement */
+#define RT_ERR_WORKSPACE 3        /* workspace missing or smaller than required */
+#define RT_ERR_CUDA 4             /* launch or driver error (see rt_last_cuda_error) */
+
+/* Device status codes written to `status`. */
+#define RT_DEV_WAIT_TIMEOUT 100 /* a bounded wait ran out; the kernel exited early */
+#define RT_DEV_BAD_INDEX 101    /* an index read from device memory was out of range */
+#define RT_DEV_OVERFLOW 102     /* a device-side capacity was exceeded */
+
+/* ABI version of this library (bumped on any signature change). */
+int rt_abi_version(void);
+
+/* Last CUDA error seen by an entry point on this thread (cudaError_t value). */
+int rt_last_cuda_error(void);
+
+/* Human-readable text for an RT_* or RT_DEV_* code. */
+const char* rt_status_string(int code);
+
+/* ------------------------------------------------------------------------
+ * KV-cache compaction after a commit.
+ * Replaces compact_tail_inplace / _compact_appended_window
+ * (ddtree.py:37-65, ddtree.py:666-686) applied to every layer's K and V by
+ * compact_dynamic_cache (ddtree.py:689-731), in ONE launch.
+ *
+ * The cache is `n_slabs` slabs (one per layer and per K/V).  Slab s starts at
+ * slabs[s] (a DEVICE array of n_slabs pointers) or, when slabs is NULL, at
+ * base + s * slab_stride.  Each slab holds n_heads heads of rows of
+ * `row_bytes` bytes at head_stride / row_stride.  Within each head the window
+ * of cur_len rows after past_len is compacted in place:
+ *     row[past_len + i] = old row[past_len + keep[i]],  i < n_keep
+ * with gather-then-scatter semantics (any order of keep is allowed).  As in
+ * the reference, nothing moves when n_keep == 0 or n_keep == cur_len.
+ * keep (int64, DEVICE) holds window-relative indices in [0, cur_len).  When
+ * n_keep_dev is non-NULL the count is read from it (<= n_keep) at run time.
+ * Limit: n_keep * row_bytes <= 200 KiB.
+ * ---------------------------------------------------------------------- */
+int rt_kv_compact(void* const* slabs, void* base, int n_slabs, int64_t slab_stride, int n_heads,
+                  int64_t head_stride, int64_t row_stride, int row_bytes, int64_t past_len, int64_t cur_len,
+                  const int64_t* keep, int n_keep, const int32_t* n_keep_dev, int* status, rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * In-place KV append into a preallocated cache.
+ * Replaces DynamicLayer.update's torch.cat of the whole cache
+ * (transformers/cache_utils.py:102-121, called from
+ * models/qwen3/modeling_qwen3.py:270-271) for one layer's K and V.
+ *
+ * Writes n_new rows per head of k_new / v_new (row r of head h at
+ * h*new_head_stride + r*new_row_stride) to rows [offset, offset+n_new) of
+ * k_cache / v_cache.  offset is read from offset_dev (int64, DEVICE) when
+ * non-NULL.  Rows past `capacity` are not written (RT_DEV_OVERFLOW).
+ * ---------------------------------------------------------------------- */
+int rt_kv_append(void* k_cache, void* v_cache, int64_t cache_head_stride, int64_t cache_row_stride,
+                 const void* k_new, const void* v_new, int64_t new_head_stride, int64_t new_row_stride,
+                 int n_heads, int n_new, int row_bytes, int64_t capacity, int64_t offset,
+                 const int64_t* offset_dev, int* status, rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Tree-verify attention (bf16, GQA, head_dim 128).
+ * Replaces sdpa_attention_forward with a tree mask
+ * (transformers/integrations/sdpa_attention.py:40-104: repeat_kv at :57-60,
+ * F.scaled_dot_product_attention at :92-101), as reached from
+ * models/qwen3/modeling_qwen3.py:273-286 with the mask that
+ * compile_ddtree_tree writes (ddtree.py:629-640).
+ *
+ * Query row (node i, head h) is at q + i*q_tok_stride + h*q_head_stride
+ * (bf16[128]).  Keys/values of kv head g are rows [0, prefix_len + n) of
+ * k/v + g*kv_head_stride (row stride kv_row_stride, bf16[128]); the cache
+ * holds kv_capacity rows per head.  Every prefix key is visible; tree key j
+ * (row prefix_len + j) is visible to node i iff bit (j % 32) of word
+ * mask[i*mask_words + j/32] is set.  out row (i, h) is written at
+ * out + i*out_tok_stride + h*out_head_stride (bf16[128]), normalised by the
+ * softmax sum.  scale multiplies QK^T (HF passes head_dim**-0.5).
+ * prefix_len is read from prefix_len_dev (int64, DEVICE) when non-NULL; then
+ * prefix_len is only an upper bound used to size the launch.
+ *
+ * Keys are split into num_splits ranges (0 = choose) whose partial results
+ * are merged by a second kernel; workspace must hold
+ * rt_tree_attn_workspace_size(...) bytes (alignment 256).  Requires
+ * num_q_heads % num_kv_heads == 0, head_dim == 128, all strides multiples of
+ * 16 bytes, q/k/v/out 16-byte aligned.  n * (num_q_heads/num_kv_heads) >= 64
+ * runs on tcgen05 (TMEM accumulators, TMA-fed K/V); smaller trees run a
+ * warp-level kernel.  `path` (0 = choose, 1 = tcgen05, 2 = warp-level)
+ * forces one of them.
+ * ---------------------------------------------------------------------- */
+size_t rt_tree_attn_workspace_size(int n, int num_q_heads, int num_kv_heads, int head_dim,
+                                   int64_t prefix_len, int num_splits);
+int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
+                 int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
+                 int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words, int n,
+                 int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads, int num_kv_heads,
+                 int head_dim, float scale, int num_splits, int path, void* workspace, size_t workspace_bytes,
+                 int* status, rt_stream_t stream);
+
+/* Number of key splits rt_tree_attn chooses for this shape (num_splits = 0). */
+int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len);
+
+/* ------------------------------------------------------------------------
+ * Packed ancestor bitmask from a dense additive mask.
+ * Replaces reading the tree block of the mask compile_ddtree_tree writes
+ * (ddtree.py:629-640): bit j of row i is set iff
+ * dense[i*ld + col0 + j] == 0 (0 = visible, finfo.min = hidden).
+ * dtype: 0 = fp32, 1 = bf16, 2 = fp16.  ld in elements.
+ * ---------------------------------------------------------------------- */
+int rt_mask_from_dense(const void* dense, int dtype, int64_t ld, int64_t col0, int n, uint32_t* mask,
+                       int mask_words, rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Draft top-k and log-normaliser.
+ * Replaces torch.topk + torch.logsumexp + the subtraction of
+ * ddtree.py:228-233 / :361-366, on the device and without the host copy.
+ *
+ * logits: rows x vocab, row stride `ld` elements, dtype 0 = fp32, 1 = bf16,
+ * 2 = fp16 (values are widened to fp32 exactly, as .float() does).
+ * Outputs: top_logp[r*k + j] = fp32(top_logit - log_z[r]), top_ids[r*k + j]
+ * (int64), log_z[r].  Order: value descending, NaN first, equal values by
+ * ascending vocabulary index.  1 <= k <= min(vocab, 1024).
+ * ---------------------------------------------------------------------- */
+size_t rt_draft_topk_workspace_size(int rows, int vocab, int k);
+int rt_draft_topk(const void* logits, int dtype, int64_t ld, int rows, int vocab, int k, float* top_logp,
+                  int64_t* top_ids, float* log_z, void* workspace, size_t workspace_bytes, rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Budgeted best-first tree expansion (one CTA per request).
+ * Replaces _build_ddtree_tree_original_heap (ddtree.py:200-308) and
+ * _build_ddtree_tree_ngram (ddtree.py:311-535, with the n-gram table of
+ * :113-151 and bonus of :154-197), i.e. build_ddtree_tree
+ * (ddtree.py:538-589) after the top-k, plus the visibility of :520-528 as a
+ * packed bitmask and the ids/positions of compile_ddtree_tree
+ * (ddtree.py:618-627).
+ *
+ * strategy: 0 = original heap, 1 = n-gram, 2 = rank-gated n-gram (the
+ * caller applies the reference's beta == 0 -> heap rule).  Scores are
+ * accumulated in binary64 in the reference's order, so the tree is
+ * bit-identical to the reference's for the same top_logp / top_ids.
+ * ctx: context ids (int64, DEVICE) read only by the n-gram strategies; its
+ * length is ctx_len, or ctx_len_dev[0] + ctx_len when ctx_len_dev is
+ * non-NULL; the last min(length, ctx_window) ids form the window
+ * (ddtree.py:135-136).
+ * log1p_table (binary64, DEVICE): log1p(c) for c = 0..table_len-1,
+ * table_len > window length.  order_weight[n-2] = longer_weight**(n-2) for
+ * n = 2..max_n.  Outputs (DEVICE): node_tokens[budget], node_depths[budget]
+ * (int64), parents[budget+1] (int32, parents[0] = -1), mask
+ * [(budget+1) x mask_words] ancestor bits, count (int32, nodes emitted).
+ * When verify_ids / verify_pos are non-NULL they receive
+ * [root, node tokens] and start + [0, depths]; root is root_dev[0] when
+ * root_dev is non-NULL, else the last context id when root < 0, else root;
+ * start is start_dev[0] when start_dev is non-NULL, else start.
+ * Limits: budget <= 1024, rows <= 64, max_n <= 8, ctx window <= 8192.
+ * ---------------------------------------------------------------------- */
+int rt_tree_build(const float* top_logp, const int64_t* top_ids, int rows, int k, int budget, int strategy,
+                  const int64_t* ctx, int64_t ctx_len, const int64_t* ctx_len_dev, int ctx_window, int max_n,
+                  double beta, int rank_cap, int min_count, int use_log_count, const double* order_weight,
+                  double max_token_bonus, const double* log1p_table, int table_len, int64_t* node_tokens,
+                  int64_t* node_depths, int32_t* parents, uint32_t* mask, int mask_words, int32_t* count,
+                  int64_t* verify_ids, int64_t* verify_pos, int64_t root, const int64_t* root_dev,
+                  int64_t start, const int64_t* start_dev, int* status, rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Exact tree walk and commit bookkeeping.
+ * Replaces follow_verified_tree (ddtree.py:650-663) and the commit of
+ * ddtree.py:906-914 / retree.py:395-403 on the device.
+ *
+ * From the root, follow the child whose token equals posterior[current]
+ * (int64[n]) while one exists (the highest-numbered such child when tokens
+ * repeat, as a dict keyed by token keeps the last).  Writes accepted node
+ * indices to accepted[0..len) (int64, accepted[0] = 0; directly usable as the
+ * `keep` of rt_kv_compact), the length to accepted_len (int32) and
+ * the target's next token to next_token.  When output_ids is non-NULL it
+ * also writes the accepted tokens (verify_ids[accepted[i]]) to
+ * output_ids[start + i] and next_token to output_ids[start + len], and
+ * advances start_dev[0] by len (start is read from start_dev).
+ * The tree is given by parents (int32[count+1]) and node tokens
+ * (int64[count]); count from count_dev when non-NULL, else `count`.
+ * ---------------------------------------------------------------------- */
+int rt_tree_walk(const int32_t* parents, const int64_t* node_tokens, int count, const int32_t* count_dev,
+                 const int64_t* posterior, int64_t* accepted, int32_t* accepted_len, int64_t* next_token,
+                 const int64_t* verify_ids, int64_t* output_ids, int64_t output_len, int64_t* start_dev,
+                 int* status, rt_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RETREE_B200_H */

@@ -1,0 +1,692 @@
+// Tree-verify attention for B200 (sm_100a): bf16 GQA, head_dim 128, packed
+// ancestor bitmask over the tree block, every prefix key visible.
+//
+// tcgen05 path (n * group >= 64 query rows per kv head)
+// ---------------------------------------------------------------------------
+// Grid (split, kv_head, m_tile).  A CTA owns 128 query rows of one kv head --
+// row r of the tile is (node (t*128+r)/group, q head kv_head*group + (..)%group),
+// so the GQA group shares every K/V tile without repeat_kv -- and a contiguous
+// range of 128-key blocks.  Six warps:
+//   warp 4  TMA producer: K and V blocks (two 64-column SW128 boxes each) into a
+//           2-stage ring, no multicast;
+//   warp 5  MMA issuer (one lane): S_j = Q K_j^T into a double-buffered TMEM
+//           tile, then O += P_{j-1} V_{j-1}; owns the TMEM allocation;
+//   warps 0-3 softmax: one query row per thread (TMEM lane), read S_j with
+//           tcgen05.ld, apply scale and the mask, online softmax in the exp2
+//           domain with a lazy (>8 in log2) rescale of O done in TMEM, write
+//           P_j as bf16 into a SW128 K-major tile for the PV MMA, and write the
+//           tile's result (normalised bf16, or fp32 partial + (m, l) when the
+//           key range is split).
+// Every mbarrier wait is bounded (common.cuh): on time-out the CTA records
+// RT_DEV_WAIT_TIMEOUT, drains what it issued, frees TMEM and exits.
+//
+// warp-level path (fewer rows): one warp per query row set, shuffle-reduced
+// dot products and online softmax; same partial format.
+//
+// Splits are merged by attn_combine_kernel (one warp per output row).
+#include <cuda.h>
+
+#include "common.cuh"
+#include "host_util.h"
+
+namespace rt {
+
+constexpr int kHD = 128;
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kAttnThreads = 192;
+constexpr uint32_t kTile = 128 * 128 * 2;  // one 128x128 bf16 tile
+constexpr uint32_t kHalf = kTile / 2;      // one 128-row x 64-column SW128 box
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kTile;
+constexpr uint32_t kOffV = 3 * kTile;
+constexpr uint32_t kOffP = 5 * kTile;
+constexpr uint32_t kOffBar = 6 * kTile;
+constexpr uint32_t kAttnSmem = kOffBar + 256 + 1024;  // + barriers + alignment slack
+constexpr uint32_t kTmemCols = 512;                   // S0 | S1 | O | spare
+constexpr float kRescaleThreshold = 8.0f;             // log2 units
+
+struct AttnParams {
+  const char* q;
+  int64_t q_tok_stride, q_head_stride;
+  char* out;
+  int64_t out_tok_stride, out_head_stride;
+  const uint32_t* mask;
+  int mask_words;
+  int n;
+  int64_t prefix_len;
+  const int64_t* prefix_len_dev;
+  int group, num_kv_heads, tiles, num_splits;
+  float scale_log2;
+  float* ws_o;     // [split][kv_head][tiles*128][128]
+  float2* ws_ml;   // [split][kv_head][tiles*128]  (m in log2 units, l)
+  int* status;
+  // warp-level path only
+  const char* k;
+  const char* v;
+  int64_t kv_head_stride, kv_row_stride;
+};
+
+struct Barriers {
+  uint64_t full_k[2], full_v[2], empty[2], s_full[2], s_free[2], p_full, o_done, fin;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ int64_t key_count(const AttnParams& p) {
+  const int64_t L = p.prefix_len_dev != nullptr ? *p.prefix_len_dev : p.prefix_len;
+  return L + p.n;
+}
+
+// Block range [b0, b1) of this split.
+__device__ __forceinline__ void split_range(int64_t total_keys, int split, int splits, int64_t blk, int64_t& b0,
+                                            int64_t& b1) {
+  const int64_t nblk = (total_keys + blk - 1) / blk;
+  const int64_t per = (nblk + splits - 1) / splits;
+  b0 = min(nblk, split * per);
+  b1 = min(nblk, b0 + per);
+}
+
+__device__ __forceinline__ void write_neutral_partial(const AttnParams& p, int split, int kvh, int row0, int rows) {
+  const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
+  for (int r = threadIdx.x; r < rows; r += blockDim.x) {
+    p.ws_ml[(static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + row0 + r] = make_float2(-INFINITY, 0.f);
+  }
+}
+
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+                        const AttnParams p) {
+  extern __shared__ unsigned char smem_raw[];
+  // 1024-byte alignment for the SW128 atoms
+  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Barriers& bar = *reinterpret_cast<Barriers*>(smem + kOffBar);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x, kvh = blockIdx.y, mt = blockIdx.z;
+  const int G = p.group;
+  const int rows_total = p.n * G;
+  const int row0 = mt * kBM;
+
+  const int64_t total_keys = key_count(p);
+  const int64_t L = total_keys - p.n;
+  int64_t b0, b1;
+  split_range(total_keys, split, p.num_splits, kBN, b0, b1);
+  const int nb = static_cast<int>(b1 - b0);
+  if (nb <= 0) {
+    if (p.num_splits > 1) write_neutral_partial(p, split, kvh, row0, min(kBM, rows_total - row0));
+    return;
+  }
+
+  if (tid == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&bar.full_k[i], 1);
+      mbar_init(&bar.full_v[i], 1);
+      mbar_init(&bar.empty[i], 1);
+      mbar_init(&bar.s_full[i], 1);
+      mbar_init(&bar.s_free[i], 128);
+    }
+    mbar_init(&bar.p_full, 128);
+    mbar_init(&bar.o_done, 1);
+    mbar_init(&bar.fin, 1);
+    bar.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(&bar.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_v);
+  }
+  // Q tile -> SW128 K-major smem (two 64-column boxes), zero rows past the tree
+  for (int c = tid; c < kBM * 16; c += kAttnThreads) {
+    const int r = c >> 4, ch = c & 15;
+    const int R = row0 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (R < rows_total) {
+      const int node = R / G, h = kvh * G + (R - node * G);
+      v = *reinterpret_cast<const uint4*>(p.q + node * p.q_tok_stride + h * p.q_head_stride + ch * 16);
+    }
+    const uint32_t off = kOffQ + (ch >> 3) * kHalf + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+    *reinterpret_cast<uint4*>(smem + off) = v;
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar.tmem_base;
+  volatile int* abort_flag = &bar.abort_flag;
+
+  if (warp == 4) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&bar.empty[st], ph ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
+        const int key0 = static_cast<int>((b0 + j) * kBN);
+        unsigned char* kd = smem + kOffK + st * kTile;
+        unsigned char* vd = smem + kOffV + st * kTile;
+        mbar_arrive_expect_tx(&bar.full_k[st], kTile);
+        tma_load_3d(kd, &tmap_k, &bar.full_k[st], 0, key0, kvh);
+        tma_load_3d(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh);
+        mbar_arrive_expect_tx(&bar.full_v[st], kTile);
+        tma_load_3d(vd, &tmap_v, &bar.full_v[st], 0, key0, kvh);
+        tma_load_3d(vd + kHalf, &tmap_v, &bar.full_v[st], 64, key0, kvh);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        // drain loads still in flight before the CTA exits
+        for (int j = max(0, issued - 2); j < issued; ++j) {
+          mbar_wait(&bar.full_k[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+          mbar_wait(&bar.full_v[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false, false);
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, kHD, false, true);
+      const uint32_t sq = smem_u32(smem + kOffQ);
+      const uint32_t sp = smem_u32(smem + kOffP);
+      bool ok = true;
+      for (int j = 0; j <= nb && ok; ++j) {
+        if (j < nb) {
+          const int st = j & 1, b = j & 1;
+          const uint32_t ph = (j >> 1) & 1;
+          ok = mbar_wait(&bar.full_k[st], ph, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT) &&
+               mbar_wait(&bar.s_free[b], ph ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sk = smem_u32(smem + kOffK + st * kTile);
+#pragma unroll
+          for (int kk = 0; kk < kHD / 16; ++kk) {
+            const uint32_t koff = (kk >> 2) * kHalf + (kk & 3) * 32;
+            umma_f16(tmem + b * kBN, smem_desc_sw128(sq + koff, 16, 1024), smem_desc_sw128(sk + koff, 16, 1024),
+                     idesc_qk, kk > 0);
+          }
+          umma_commit(&bar.s_full[b]);
+        }
+        if (j >= 1) {
+          const int jp = j - 1, stp = jp & 1;
+          ok = mbar_wait(&bar.p_full, jp & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT) &&
+               mbar_wait(&bar.full_v[stp], (jp >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t sv = smem_u32(smem + kOffV + stp * kTile);
+#pragma unroll
+          for (int kk = 0; kk < kBN / 16; ++kk) {
+            const uint32_t poff = (kk >> 2) * kHalf + (kk & 3) * 32;
+            // V is MN-major: 16 keys = two 8-row SW128 atoms (1024 B apart);
+            // the second 64-column half of head_dim sits one box (LBO) away.
+            umma_f16(tmem + 2 * kBN, smem_desc_sw128(sp + poff, 16, 1024),
+                     smem_desc_sw128(sv + kk * 2048, kHalf, 1024), idesc_pv, (jp > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(&bar.o_done);
+          umma_commit(&bar.empty[stp]);
+        }
+      }
+      // all issued MMAs complete before TMEM is released
+      umma_commit(&bar.fin);
+      mbar_wait(&bar.fin, 0, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+    }
+  } else {
+    // ---------------- softmax / epilogue (warps 0-3) ----------------
+    const int r = tid;  // TMEM lane == tile row
+    const int R = row0 + r;
+    const bool valid = R < rows_total;
+    const int node = valid ? R / G : 0;
+    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t* mrow = p.mask + static_cast<int64_t>(node) * p.mask_words;
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    uint32_t sreg[4][32];
+    for (int j = 0; j < nb; ++j) {
+      const int b = j & 1;
+      ok = mbar_wait(&bar.s_full[b], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+      if (!ok) break;
+      tc_fence_after();
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + b * kBN + c4 * 32, sreg[c4]);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&bar.s_free[b]);
+      const int64_t key0 = (b0 + j) * kBN;
+      float mloc = -INFINITY;
+      if (valid && key0 + kBN <= L) {
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const float x = __uint_as_float(sreg[c4][c]) * p.scale_log2;
+            sreg[c4][c] = __float_as_uint(x);
+            mloc = fmaxf(mloc, x);
+          }
+      } else {
+        // block reaches the tree keys (or the end): visibility per column
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int64_t key = key0 + c4 * 32 + c;
+            bool vis = false;
+            if (valid) {
+              if (key < L) {
+                vis = true;
+              } else if (key < total_keys) {
+                const int64_t t = key - L;
+                vis = (mrow[t >> 5] >> (t & 31)) & 1u;
+              }
+            }
+            const float x = vis ? __uint_as_float(sreg[c4][c]) * p.scale_log2 : -INFINITY;
+            sreg[c4][c] = __float_as_uint(x);
+            mloc = fmaxf(mloc, x);
+          }
+        }
+      }
+      const float m_new = fmaxf(m, mloc);
+      const bool need = m_new > m + kRescaleThreshold;  // false while both are -inf
+      if (j > 0) {
+        ok = mbar_wait(&bar.o_done, (j - 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(0xFFFFFFFFu, need)) {
+          const float f = need ? ex2(m - m_new) : 1.f;  // ex2(-inf) = 0 when m was -inf
+          uint32_t o[32];
+#pragma unroll
+          for (int c4 = 0; c4 < 4; ++c4) {
+            tmem_ld32(tmem + lane_base + 2 * kBN + c4 * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
+            tmem_st32(tmem + lane_base + 2 * kBN + c4 * 32, o);
+          }
+          tmem_wait_st();
+          if (need) l *= f;
+        }
+      }
+      if (need) m = m_new;
+      const float mu = (m == -INFINITY) ? 0.f : m;
+      // P = exp2(s - m) as bf16, SW128 K-major (keys 0-63 | 64-127)
+      float lsum = 0.f;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {  // 8 keys = one 16-byte chunk
+          float e[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) {
+            e[t] = ex2(__uint_as_float(sreg[c4][q * 8 + t]) - mu);
+            lsum += e[t];
+          }
+          const int col = c4 * 32 + q * 8;
+          const int ch = (col & 63) >> 3;
+          const uint32_t off = kOffP + (col >> 6) * kHalf + r * 128 + ((ch ^ (r & 7)) << 4);
+          uint4 pk;
+          pk.x = pack_bf16x2(e[0], e[1]);
+          pk.y = pack_bf16x2(e[2], e[3]);
+          pk.z = pack_bf16x2(e[4], e[5]);
+          pk.w = pack_bf16x2(e[6], e[7]);
+          *reinterpret_cast<uint4*>(smem + off) = pk;
+        }
+      }
+      l += lsum;
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&bar.p_full);
+    }
+    if (ok) ok = mbar_wait(&bar.o_done, (nb - 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+    if (ok) {
+      tc_fence_after();
+      const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
+      const int h = valid ? kvh * G + (R - node * G) : 0;
+#pragma unroll
+      for (int c4 = 0; c4 < 4; ++c4) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_base + 2 * kBN + c4 * 32, o);
+        tmem_wait_ld();
+        if (!valid) continue;
+        if (p.num_splits == 1) {
+          const float inv = 1.f / l;
+          char* dst = p.out + node * p.out_tok_stride + h * p.out_head_stride + c4 * 64;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 pk;
+            pk.x = pack_bf16x2(__uint_as_float(o[q * 8 + 0]) * inv, __uint_as_float(o[q * 8 + 1]) * inv);
+            pk.y = pack_bf16x2(__uint_as_float(o[q * 8 + 2]) * inv, __uint_as_float(o[q * 8 + 3]) * inv);
+            pk.z = pack_bf16x2(__uint_as_float(o[q * 8 + 4]) * inv, __uint_as_float(o[q * 8 + 5]) * inv);
+            pk.w = pack_bf16x2(__uint_as_float(o[q * 8 + 6]) * inv, __uint_as_float(o[q * 8 + 7]) * inv);
+            *reinterpret_cast<uint4*>(dst + q * 16) = pk;
+          }
+        } else {
+          float* dst = p.ws_o + ((static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + R) * kHD + c4 * 32;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(dst + q * 4) =
+                make_float4(__uint_as_float(o[q * 4]), __uint_as_float(o[q * 4 + 1]), __uint_as_float(o[q * 4 + 2]),
+                            __uint_as_float(o[q * 4 + 3]));
+        }
+      }
+      if (valid && p.num_splits > 1)
+        p.ws_ml[(static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + R] = make_float2(m, l);
+    }
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 5) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Warp-level path: CTA = (split, kv head), 4 warps, K/V blocks of 64 keys in
+// shared memory; warp w handles query rows w, w+4, ...  Each lane owns 4 of the
+// 128 dims; dot products are shuffle-reduced.
+// ---------------------------------------------------------------------------
+constexpr int kSimtKeys = 64;
+
+__global__ void __launch_bounds__(128) tree_attn_simt_kernel(const AttnParams p) {
+  __shared__ __align__(16) __nv_bfloat16 ks[kSimtKeys][kHD];
+  __shared__ __align__(16) __nv_bfloat16 vs[kSimtKeys][kHD];
+  const int split = blockIdx.x, kvh = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.group, rows = p.n * G;
+  const int64_t total_keys = key_count(p);
+  const int64_t L = total_keys - p.n;
+  int64_t b0, b1;
+  split_range(total_keys, split, p.num_splits, kSimtKeys, b0, b1);
+  constexpr int kMaxRowsPerWarp = 16;
+  float qv[kMaxRowsPerWarp][4];
+  float acc[kMaxRowsPerWarp][4];
+  float m[kMaxRowsPerWarp], l[kMaxRowsPerWarp];
+#pragma unroll
+  for (int i = 0; i < kMaxRowsPerWarp; ++i) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+    const int R = warp + 4 * i;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+      acc[i][d] = 0.f;
+      qv[i][d] = 0.f;
+    }
+    if (R < rows) {
+      const int node = R / G, h = kvh * G + (R - node * G);
+      const __nv_bfloat16* qp =
+          reinterpret_cast<const __nv_bfloat16*>(p.q + node * p.q_tok_stride + h * p.q_head_stride) + lane * 4;
+#pragma unroll
+      for (int d = 0; d < 4; ++d) qv[i][d] = __bfloat162float(qp[d]) * p.scale_log2;
+    }
+  }
+  for (int64_t blk = b0; blk < b1; ++blk) {
+    const int64_t key0 = blk * kSimtKeys;
+    __syncthreads();
+    for (int c = threadIdx.x; c < kSimtKeys * 16; c += 128) {
+      const int kr = c >> 4, ch = c & 15;
+      const int64_t key = key0 + kr;
+      uint4 kv4 = make_uint4(0, 0, 0, 0), vv4 = make_uint4(0, 0, 0, 0);
+      if (key < total_keys) {
+        kv4 = *reinterpret_cast<const uint4*>(p.k + kvh * p.kv_head_stride + key * p.kv_row_stride + ch * 16);
+        vv4 = *reinterpret_cast<const uint4*>(p.v + kvh * p.kv_head_stride + key * p.kv_row_stride + ch * 16);
+      }
+      *reinterpret_cast<uint4*>(&ks[kr][ch * 8]) = kv4;
+      *reinterpret_cast<uint4*>(&vs[kr][ch * 8]) = vv4;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxRowsPerWarp; ++i) {
+      const int R = warp + 4 * i;
+      if (R >= rows) break;
+      const int node = R / G;
+      // scores of keys `lane` and `lane + 32`
+      float s2[2];
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float mine = -INFINITY;
+        for (int kk = 0; kk < 32; ++kk) {
+          const int kr = half * 32 + kk;
+          const __nv_bfloat16* kp = &ks[kr][lane * 4];
+          float d = qv[i][0] * __bfloat162float(kp[0]) + qv[i][1] * __bfloat162float(kp[1]) +
+                    qv[i][2] * __bfloat162float(kp[2]) + qv[i][3] * __bfloat162float(kp[3]);
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(0xFFFFFFFFu, d, o);
+          if (kk == lane) mine = d;
+        }
+        const int64_t key = key0 + half * 32 + lane;
+        bool vis = key < L;
+        if (!vis && key < total_keys) {
+          const int64_t t = key - L;
+          vis = (p.mask[static_cast<int64_t>(node) * p.mask_words + (t >> 5)] >> (t & 31)) & 1u;
+        }
+        s2[half] = vis ? mine : -INFINITY;
+      }
+      float bm = fmaxf(s2[0], s2[1]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xFFFFFFFFu, bm, o));
+      const float m_new = fmaxf(m[i], bm);
+      const float mu = m_new == -INFINITY ? 0.f : m_new;
+      const float f = ex2(m[i] - mu);
+      const float e0 = ex2(s2[0] - mu), e1 = ex2(s2[1] - mu);
+      float es = e0 + e1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) es += __shfl_xor_sync(0xFFFFFFFFu, es, o);
+      l[i] = l[i] * f + es;
+      m[i] = m_new;
+#pragma unroll
+      for (int d = 0; d < 4; ++d) acc[i][d] *= f;
+      for (int kk = 0; kk < kSimtKeys; ++kk) {
+        const float pk = __shfl_sync(0xFFFFFFFFu, kk < 32 ? e0 : e1, kk & 31);
+        const __nv_bfloat16* vp = &vs[kk][lane * 4];
+#pragma unroll
+        for (int d = 0; d < 4; ++d) acc[i][d] += pk * __bfloat162float(vp[d]);
+      }
+    }
+  }
+  const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
+#pragma unroll
+  for (int i = 0; i < kMaxRowsPerWarp; ++i) {
+    const int R = warp + 4 * i;
+    if (R >= rows) break;
+    const int node = R / G, h = kvh * G + (R - node * G);
+    if (p.num_splits == 1) {
+      const float inv = 1.f / l[i];
+      uint2 pk;
+      pk.x = pack_bf16x2(acc[i][0] * inv, acc[i][1] * inv);
+      pk.y = pack_bf16x2(acc[i][2] * inv, acc[i][3] * inv);
+      *reinterpret_cast<uint2*>(p.out + node * p.out_tok_stride + h * p.out_head_stride + lane * 8) = pk;
+    } else {
+      const int64_t idx = (static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + R;
+      *reinterpret_cast<float4*>(p.ws_o + idx * kHD + lane * 4) =
+          make_float4(acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      if (lane == 0) p.ws_ml[idx] = make_float2(m[i], l[i]);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Split merge: one warp per (kv head, tile row); lane owns 4 dims.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int rows = p.n * p.group;
+  if (gw >= p.num_kv_heads * rows) return;
+  const int kvh = gw / rows, R = gw - kvh * rows;
+  const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
+  float M = -INFINITY;
+  for (int s = 0; s < p.num_splits; ++s)
+    M = fmaxf(M, p.ws_ml[(static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R].x);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float lsum = 0.f;
+  if (M > -INFINITY) {
+    for (int s = 0; s < p.num_splits; ++s) {
+      const int64_t idx = (static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R;
+      const float2 ml = p.ws_ml[idx];
+      if (ml.x == -INFINITY) continue;
+      const float w = ex2(ml.x - M);
+      const float4 o = *reinterpret_cast<const float4*>(p.ws_o + idx * kHD + lane * 4);
+      acc.x += w * o.x;
+      acc.y += w * o.y;
+      acc.z += w * o.z;
+      acc.w += w * o.w;
+      lsum += w * ml.y;
+    }
+  }
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  const int node = R / p.group, h = kvh * p.group + (R - node * p.group);
+  uint2 pk;
+  pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+  pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(p.out + node * p.out_tok_stride + h * p.out_head_stride + lane * 8) = pk;
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+static int make_kv_tmap(CUtensorMap* m, const void* base, int64_t head_stride, int64_t row_stride, int64_t capacity,
+                        int heads) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return RT_ERR_CUDA;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(capacity),
+                              static_cast<cuuint64_t>(heads)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(row_stride), static_cast<cuuint64_t>(head_stride)};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBN), 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? RT_OK : RT_ERR_INVALID_ARGUMENT;
+}
+
+static int tiles_for(int n, int G) { return (n * G + kBM - 1) / kBM; }
+
+static int default_splits(int n, int G, int hkv, int64_t prefix_len, bool tc) {
+  const int64_t keys = prefix_len + n;
+  const int blk = tc ? kBN : kSimtKeys;
+  const int64_t nblk = (keys + blk - 1) / blk;
+  const int tiles = tc ? tiles_for(n, G) : 1;
+  const int64_t ctas = static_cast<int64_t>(hkv) * tiles;
+  const int64_t target = std::min<int64_t>(256, (148 + ctas - 1) / ctas);  // about one CTA per SM
+  const int64_t per = std::max<int64_t>(1, (nblk + target - 1) / target);    // blocks per split
+  return static_cast<int>(std::max<int64_t>(1, (nblk + per - 1) / per));
+}
+
+static bool use_tc(int n, int G, int path) { return path == 1 || (path == 0 && n * G >= 64); }
+
+}  // namespace rt
+
+using namespace rt;
+
+extern "C" int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len) {
+  if (n <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return 1;
+  const int G = num_q_heads / num_kv_heads;
+  return default_splits(n, G, num_kv_heads, prefix_len, use_tc(n, G, 0));
+}
+
+extern "C" size_t rt_tree_attn_workspace_size(int n, int num_q_heads, int num_kv_heads, int head_dim,
+                                              int64_t prefix_len, int num_splits) {
+  if (n <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || head_dim != kHD) return 0;
+  const int G = num_q_heads / num_kv_heads;
+  if (num_splits <= 0) num_splits = default_splits(n, G, num_kv_heads, prefix_len, use_tc(n, G, 0));
+  if (num_splits == 1) return 0;
+  const size_t rows_ws = static_cast<size_t>(tiles_for(n, G)) * kBM;
+  const size_t slots = static_cast<size_t>(num_splits) * num_kv_heads * rows_ws;
+  return align_up(slots * kHD * 4, 256) + align_up(slots * 8, 256);
+}
+
+extern "C" int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
+                            int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
+                            int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words,
+                            int n, int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads,
+                            int num_kv_heads, int head_dim, float scale, int num_splits, int path, void* workspace,
+                            size_t workspace_bytes, int* status, rt_stream_t stream) {
+  if (!q || !k || !v || !out || !mask) return RT_ERR_INVALID_ARGUMENT;
+  if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || prefix_len < 0)
+    return RT_ERR_INVALID_ARGUMENT;
+  if (head_dim != kHD) return RT_ERR_UNSUPPORTED;
+  if (mask_words < (n + 31) / 32) return RT_ERR_INVALID_ARGUMENT;
+  if (prefix_len_dev == nullptr && prefix_len + n > kv_capacity) return RT_ERR_INVALID_ARGUMENT;
+  const uint64_t align_bits = reinterpret_cast<uint64_t>(q) | reinterpret_cast<uint64_t>(k) |
+                              reinterpret_cast<uint64_t>(v) | reinterpret_cast<uint64_t>(out) |
+                              static_cast<uint64_t>(q_tok_stride) | static_cast<uint64_t>(q_head_stride) |
+                              static_cast<uint64_t>(kv_head_stride) | static_cast<uint64_t>(kv_row_stride) |
+                              static_cast<uint64_t>(out_tok_stride) | static_cast<uint64_t>(out_head_stride);
+  if (align_bits & 15) return RT_ERR_INVALID_ARGUMENT;
+  if (path < 0 || path > 2) return RT_ERR_INVALID_ARGUMENT;
+  const int G = num_q_heads / num_kv_heads;
+  const bool tc = use_tc(n, G, path);
+  if (!tc && n * G > 64) return RT_ERR_UNSUPPORTED;  // warp-level path holds <= 64 rows
+  if (kv_capacity > INT32_MAX) return RT_ERR_UNSUPPORTED;
+  if (num_splits <= 0) num_splits = default_splits(n, G, num_kv_heads, prefix_len, tc);
+  AttnParams p{};
+  p.q = static_cast<const char*>(q);
+  p.q_tok_stride = q_tok_stride;
+  p.q_head_stride = q_head_stride;
+  p.out = static_cast<char*>(out);
+  p.out_tok_stride = out_tok_stride;
+  p.out_head_stride = out_head_stride;
+  p.mask = mask;
+  p.mask_words = mask_words;
+  p.n = n;
+  p.prefix_len = prefix_len;
+  p.prefix_len_dev = prefix_len_dev;
+  p.group = G;
+  p.num_kv_heads = num_kv_heads;
+  p.tiles = tiles_for(n, G);
+  p.num_splits = num_splits;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.status = status;
+  p.k = static_cast<const char*>(k);
+  p.v = static_cast<const char*>(v);
+  p.kv_head_stride = kv_head_stride;
+  p.kv_row_stride = kv_row_stride;
+  if (num_splits > 1) {
+    const size_t need = rt_tree_attn_workspace_size(n, num_q_heads, num_kv_heads, head_dim, prefix_len, num_splits);
+    if (workspace == nullptr || workspace_bytes < need) return RT_ERR_WORKSPACE;
+    const size_t rows_ws = static_cast<size_t>(p.tiles) * kBM;
+    const size_t slots = static_cast<size_t>(num_splits) * num_kv_heads * rows_ws;
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_ml = reinterpret_cast<float2*>(static_cast<char*>(workspace) + align_up(slots * kHD * 4, 256));
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (tc) {
+    CUtensorMap tk, tv;
+    int rc = make_kv_tmap(&tk, k, kv_head_stride, kv_row_stride, kv_capacity, num_kv_heads);
+    if (rc != RT_OK) return rc;
+    rc = make_kv_tmap(&tv, v, kv_head_stride, kv_row_stride, kv_capacity, num_kv_heads);
+    if (rc != RT_OK) return rc;
+    set_smem_limit(tree_attn_tc_kernel, kAttnSmem);
+    const dim3 grid(num_splits, num_kv_heads, p.tiles);
+    tree_attn_tc_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(tk, tv, p);
+  } else {
+    const dim3 grid(num_splits, num_kv_heads);
+    tree_attn_simt_kernel<<<grid, 128, 0, s>>>(p);
+  }
+  int rc = check_launch();
+  if (rc != RT_OK || num_splits == 1) return rc;
+  const int warps = num_kv_heads * n * G;
+  attn_combine_kernel<<<(warps + 3) / 4, 128, 0, s>>>(p);
+  return check_launch();
+}

@@ -1,0 +1,328 @@
+"""Torch-tensor wrappers over the C-ABI kernels.
+
+PyTorch supplies device memory and the current stream; every computation is a
+call into ``libretree_b200.so``.  Inputs must already be CUDA tensors: there
+is no CPU path, and a missing library raises (``retree_b200._lib.load``).
+"""
+
+from __future__ import annotations
+
+import threading
+
+import numpy as np
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("retree_b200 kernels take CUDA tensors (no CPU path)")
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _DeviceState:
+    """Per-device scratch and status words (grown on demand, never shrunk)."""
+
+    def __init__(self):
+        self.lock = threading.Lock()
+        self.bufs: dict = {}
+
+    def buffer(self, device, name: str, nbytes: int) -> torch.Tensor:
+        key = (torch.device(device).index, name)
+        with self.lock:
+            b = self.bufs.get(key)
+            if b is None or b.numel() < nbytes:
+                b = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+                self.bufs[key] = b
+            return b
+
+    def status(self, device) -> torch.Tensor:
+        key = (torch.device(device).index, "__status__")
+        with self.lock:
+            s = self.bufs.get(key)
+            if s is None:
+                s = torch.zeros(1, dtype=torch.int32, device=device)
+                self.bufs[key] = s
+            return s
+
+
+_STATE = _DeviceState()
+
+
+def status_tensor(device) -> torch.Tensor:
+    """The device status word the kernels of this process report into."""
+    return _STATE.status(device)
+
+
+def check_device_status(device, reset: bool = True) -> None:
+    """Synchronise on the status word and raise if a kernel reported an error."""
+    s = _STATE.status(device)
+    code = int(s.item())
+    if reset and code:
+        s.zero_()
+    if code:
+        raise RuntimeError(f"retree_b200 kernel reported: {_lib.status_string(code)}")
+
+
+# ---------------------------------------------------------------------------
+# KV cache
+# ---------------------------------------------------------------------------
+def kv_compact(tensors, past_length: int, keep: torch.Tensor, cur_length: int | None = None,
+               n_keep_dev: torch.Tensor | None = None, n_keep: int | None = None) -> None:
+    """In-place compaction of appended rows (ddtree.py:666-731 semantics).
+
+    ``tensors``: one ``[..., S, D]`` tensor or a list of them.  All leading
+    dims of a tensor are folded into one head axis when their strides allow
+    (a whole ``[layers*2, heads, S, D]`` slab then moves in ONE launch).
+    ``keep``: int64 CUDA tensor of window-relative indices; ``n_keep_dev``
+    (int32[1], optional) supplies the count at run time.
+    """
+    lib = _lib.load()
+    group = [tensors] if isinstance(tensors, torch.Tensor) else list(tensors)
+    if not group:
+        return
+    _require_cuda(keep, *group)
+    if keep.dtype != torch.int64:
+        raise RuntimeError("keep_current_indices must have dtype torch.long")
+    nk = int(keep.numel()) if n_keep is None else int(n_keep)
+    for t in group:
+        if t.dim() < 2:
+            raise RuntimeError("cache_tensor must have rank >= 2")
+        seq = t.shape[-2]
+        if past_length < 0 or past_length > seq:
+            raise RuntimeError("past_length exceeds cache sequence length")
+        cur = (seq - past_length) if cur_length is None else int(cur_length)
+        if cur <= 0:
+            continue
+        if t.stride(-1) != 1:
+            raise RuntimeError("cache rows must be contiguous")
+        try:
+            v = t.view(-1, seq, t.shape[-1])
+        except RuntimeError:
+            kv_compact(list(t.unbind(0)), past_length, keep, cur_length, n_keep_dev, n_keep)
+            continue
+        es = v.element_size()
+        rc = lib.rt_kv_compact(None, v.data_ptr(), 1, 0, v.shape[0], v.stride(0) * es, v.stride(1) * es,
+                               v.shape[2] * es, int(past_length), cur, keep.data_ptr(), nk, _ptr(n_keep_dev),
+                               _STATE.status(t.device).data_ptr(), _stream(t.device))
+        _lib.check(rc, "rt_kv_compact")
+
+
+def kv_append(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
+              offset: int = 0, offset_dev: torch.Tensor | None = None) -> None:
+    """Write ``[heads, n, D]`` new rows at ``offset`` of ``[heads, cap, D]`` caches (views allowed)."""
+    lib = _lib.load()
+    _require_cuda(k_cache, v_cache, k_new, v_new)
+    k_cache, v_cache = _as3(k_cache), _as3(v_cache)
+    k_new, v_new = _as3(k_new), _as3(v_new)
+    if k_new.stride() != v_new.stride() or k_cache.stride() != v_cache.stride():
+        raise RuntimeError("K and V must share strides")
+    es = k_cache.element_size()
+    heads, n, d = k_new.shape
+    rc = lib.rt_kv_append(k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0) * es, k_cache.stride(1) * es,
+                          k_new.data_ptr(), v_new.data_ptr(), k_new.stride(0) * es, k_new.stride(1) * es, heads, n,
+                          d * es, k_cache.shape[1], int(offset), _ptr(offset_dev),
+                          _STATE.status(k_cache.device).data_ptr(), _stream(k_cache.device))
+    _lib.check(rc, "rt_kv_append")
+
+
+def _as3(t: torch.Tensor) -> torch.Tensor:
+    if t.dim() == 4:
+        if t.shape[0] != 1:
+            raise RuntimeError("batch size 1 only")
+        t = t[0]
+    if t.dim() != 3 or t.stride(-1) != 1:
+        raise RuntimeError("expected [heads, seq, head_dim] with contiguous head_dim")
+    return t
+
+
+# ---------------------------------------------------------------------------
+# Tree-verify attention
+# ---------------------------------------------------------------------------
+def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits: torch.Tensor, prefix_len: int,
+                   scale: float | None = None, out: torch.Tensor | None = None, num_splits: int = 0,
+                   path: int = 0, prefix_len_dev: torch.Tensor | None = None,
+                   kv_capacity: int | None = None) -> torch.Tensor:
+    """Masked GQA attention of n tree nodes over ``[prefix ; tree block]``.
+
+    q: ``[n, Hq, D]`` or HF's ``[1, Hq, n, D]``; k, v: ``[Hkv, S, D]`` or
+    ``[1, Hkv, S, D]`` (rows ``[0, prefix_len + n)`` are used);
+    mask_bits: int32 ``[n, W]`` ancestor bits of the tree block.
+    Returns ``out`` ``[n, Hq, D]`` bf16 (HF's ``[1, n, Hq, D]`` after unsqueeze).
+    """
+    lib = _lib.load()
+    _require_cuda(q, k, v, mask_bits)
+    if q.dim() == 4:
+        if q.shape[0] != 1:
+            raise RuntimeError("batch size 1 only")
+        q = q[0].transpose(0, 1)  # [n, Hq, D] view
+    k, v = _as3(k), _as3(v)
+    if k.stride() != v.stride():
+        raise RuntimeError("K and V must share strides")
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16:
+        raise RuntimeError("tree attention runs on bf16 q/k/v")
+    n, hq, d = q.shape
+    hkv = k.shape[0]
+    if out is None:
+        out = torch.empty((n, hq, d), dtype=torch.bfloat16, device=q.device)
+    es = 2
+    mask_bits = mask_bits if mask_bits.dim() == 2 else mask_bits.reshape(n, -1)
+    if mask_bits.stride(-1) != 1:
+        mask_bits = mask_bits.contiguous()
+    words = mask_bits.stride(0)
+    scale = d ** -0.5 if scale is None else float(scale)
+    cap = k.shape[1] if kv_capacity is None else int(kv_capacity)
+    splits = num_splits if num_splits > 0 else lib.rt_tree_attn_default_splits(n, hq, hkv, int(prefix_len))
+    ws_bytes = lib.rt_tree_attn_workspace_size(n, hq, hkv, d, int(prefix_len), splits)
+    ws = _STATE.buffer(q.device, "attn_ws", ws_bytes) if ws_bytes else None
+    rc = lib.rt_tree_attn(q.data_ptr(), q.stride(0) * es, q.stride(1) * es, k.data_ptr(), v.data_ptr(),
+                          k.stride(0) * es, k.stride(1) * es, cap, out.data_ptr(), out.stride(0) * es,
+                          out.stride(1) * es, mask_bits.data_ptr(), words, n, int(prefix_len), _ptr(prefix_len_dev),
+                          hq, hkv, d, scale, splits, path, _ptr(ws), ws_bytes,
+                          _STATE.status(q.device).data_ptr(), _stream(q.device))
+    _lib.check(rc, "rt_tree_attn")
+    return out
+
+
+def mask_from_dense(dense: torch.Tensor, col0: int, n: int, words: int | None = None) -> torch.Tensor:
+    """Packed bits of the tree block of a dense additive mask (0 = visible)."""
+    lib = _lib.load()
+    _require_cuda(dense)
+    d2 = dense.reshape(-1, dense.shape[-1]) if dense.dim() > 2 else dense
+    if d2.stride(-1) != 1:
+        raise RuntimeError("dense mask rows must be contiguous")
+    w = (n + 31) // 32 if words is None else words
+    bits = torch.empty((n, w), dtype=torch.int32, device=dense.device)
+    rc = lib.rt_mask_from_dense(d2.data_ptr(), _DTYPE_CODE[d2.dtype], d2.stride(0), int(col0), n, bits.data_ptr(),
+                                w, _stream(dense.device))
+    _lib.check(rc, "rt_mask_from_dense")
+    return bits
+
+
+# ---------------------------------------------------------------------------
+# Draft top-k and tree construction
+# ---------------------------------------------------------------------------
+def draft_topk(logits: torch.Tensor, k: int, out=None):
+    """``(top_logp f32[R,k], top_ids i64[R,k], log_z f32[R])`` of ``[R, V]`` logits on the device."""
+    lib = _lib.load()
+    _require_cuda(logits)
+    if logits.dim() != 2 or logits.stride(-1) != 1:
+        raise RuntimeError("logits must be [rows, vocab] with contiguous rows")
+    rows, vocab = logits.shape
+    dev = logits.device
+    if out is None:
+        out = (torch.empty((rows, k), dtype=torch.float32, device=dev),
+               torch.empty((rows, k), dtype=torch.int64, device=dev),
+               torch.empty((rows,), dtype=torch.float32, device=dev))
+    ws_bytes = lib.rt_draft_topk_workspace_size(rows, vocab, k)
+    ws = _STATE.buffer(dev, "topk_ws", ws_bytes)
+    rc = lib.rt_draft_topk(logits.data_ptr(), _DTYPE_CODE[logits.dtype], logits.stride(0), rows, vocab, k,
+                           out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), ws.data_ptr(), ws_bytes,
+                           _stream(dev))
+    _lib.check(rc, "rt_draft_topk")
+    return out
+
+
+STRATEGY_CODE = {"heap": 0, "ngram": 1, "rank_gated_ngram": 2}
+
+_LOG1P_CACHE: dict = {}
+
+
+def log1p_table(device, n: int) -> torch.Tensor:
+    """``np.log1p(c)`` for c = 0..n as binary64 on ``device`` (the reference's bonus base)."""
+    key = (torch.device(device).index, n)
+    t = _LOG1P_CACHE.get(key)
+    if t is None:
+        t = torch.from_numpy(np.log1p(np.arange(n + 1, dtype=np.float64))).to(device)
+        _LOG1P_CACHE[key] = t
+    return t
+
+
+def tree_build(top_logp: torch.Tensor, top_ids: torch.Tensor, budget: int, strategy: str, params,
+               ctx: torch.Tensor | None = None, ctx_len_dev: torch.Tensor | None = None, ctx_len: int | None = None,
+               out: dict | None = None, root: int = -1, root_dev=None, start: int = 0, start_dev=None,
+               mask_words: int | None = None) -> dict:
+    """Best-first expansion on the device; returns a dict of device tensors.
+
+    Keys: tokens i64[budget], depths i64[budget], parents i32[budget+1],
+    mask i32[budget+1, W], count i32[1], verify_ids i64[budget+1],
+    verify_pos i64[budget+1].  ``params``: oracle-compatible n-gram knobs
+    (``max_n, beta, rank_cap, min_count, context_window, use_log_count,
+    longer_weight, max_token_bonus``).
+    """
+    lib = _lib.load()
+    _require_cuda(top_logp, top_ids, ctx)
+    dev = top_logp.device
+    rows, k = top_logp.shape
+    code = STRATEGY_CODE[strategy]
+    w = (budget + 1 + 31) // 32 if mask_words is None else mask_words
+    if out is None:
+        out = dict(
+            tokens=torch.empty(max(budget, 1), dtype=torch.int64, device=dev),
+            depths=torch.empty(max(budget, 1), dtype=torch.int64, device=dev),
+            parents=torch.empty(budget + 1, dtype=torch.int32, device=dev),
+            mask=torch.empty((budget + 1, w), dtype=torch.int32, device=dev),
+            count=torch.empty(1, dtype=torch.int32, device=dev),
+            verify_ids=torch.empty(budget + 1, dtype=torch.int64, device=dev),
+            verify_pos=torch.empty(budget + 1, dtype=torch.int64, device=dev),
+        )
+    max_n = int(params.max_n) if code else 2
+    ow = torch.tensor([float(params.longer_weight ** max(0, n - 2)) for n in range(2, max_n + 1)],
+                      dtype=torch.float64, device=dev)
+    window = int(params.context_window)
+    if ctx is not None:
+        clen = int(ctx.numel()) if ctx_len is None else int(ctx_len)
+    else:
+        clen = 0
+    table_n = (window if window > 0 else max(clen, 1)) if ctx_len_dev is not None else \
+        (min(clen, window) if window > 0 else clen)
+    table = log1p_table(dev, max(table_n, 1) + 1)
+    rc = lib.rt_tree_build(
+        top_logp.data_ptr(), top_ids.data_ptr(), rows, k, int(budget), code, _ptr(ctx), clen, _ptr(ctx_len_dev),
+        window, max_n, float(params.beta), int(params.rank_cap), int(params.min_count), int(bool(params.use_log_count)),
+        ow.data_ptr(), float(params.max_token_bonus), table.data_ptr(), int(table.numel()),
+        out["tokens"].data_ptr(), out["depths"].data_ptr(), out["parents"].data_ptr(), out["mask"].data_ptr(), w,
+        out["count"].data_ptr(), _ptr(out.get("verify_ids")), _ptr(out.get("verify_pos")), int(root), _ptr(root_dev),
+        int(start), _ptr(start_dev), _STATE.status(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "rt_tree_build")
+    out["_keep_alive"] = (ow, table)
+    return out
+
+
+def tree_walk(parents: torch.Tensor, tokens: torch.Tensor, posterior: torch.Tensor, count: int | None = None,
+              count_dev: torch.Tensor | None = None, out: dict | None = None, verify_ids=None, output_ids=None,
+              start_dev=None) -> dict:
+    """Exact walk on the device; returns ``accepted`` i64[n], ``accepted_len`` i32[1], ``next_token`` i64[1]."""
+    lib = _lib.load()
+    _require_cuda(parents, tokens, posterior)
+    dev = parents.device
+    n = parents.numel()
+    if out is None:
+        out = dict(accepted=torch.empty(n, dtype=torch.int64, device=dev),
+                   accepted_len=torch.empty(1, dtype=torch.int32, device=dev),
+                   next_token=torch.empty(1, dtype=torch.int64, device=dev))
+    cnt = (n - 1) if count is None else int(count)
+    post = posterior.reshape(-1)
+    if post.dtype != torch.int64:
+        post = post.to(torch.int64)
+    rc = lib.rt_tree_walk(parents.data_ptr(), tokens.data_ptr(), cnt, _ptr(count_dev), post.data_ptr(),
+                          out["accepted"].data_ptr(), out["accepted_len"].data_ptr(), out["next_token"].data_ptr(),
+                          _ptr(verify_ids), _ptr(output_ids), 0 if output_ids is None else output_ids.numel(),
+                          _ptr(start_dev), _STATE.status(dev).data_ptr(), _stream(dev))
+    _lib.check(rc, "rt_tree_walk")
+    return out
+
+
+__all__ = ["kv_compact", "kv_append", "tree_attention", "mask_from_dense", "draft_topk", "tree_build",
+           "tree_walk", "log1p_table", "status_tensor", "check_device_status", "STRATEGY_CODE"]

@@ -1,0 +1,79 @@
+"""The C-ABI library loads and exports exactly what include/retree_b200.h declares (CPU only)."""
+
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from retree_b200 import _lib, kernels
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "retree_b200.h"
+
+
+def _declared():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    decls = {}
+    for m in re.finditer(r"^\s*(?:const\s+)?[\w\s\*]+?\b(rt_\w+)\s*\(([^;]*?)\)\s*;", text, flags=re.M | re.S):
+        args = [a.strip() for a in m.group(2).split(",")]
+        decls[m.group(1)] = [] if args == ["void"] else args
+    return decls
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    lib = _lib.load()
+    decls = _declared()
+    assert decls, "no declarations parsed"
+    for name in decls:
+        assert hasattr(lib, name), name
+    assert set(decls) == set(_lib.SIGNATURES)
+    assert lib.rt_abi_version() == 1
+
+
+def test_ctypes_signatures_match_header():
+    import ctypes
+    decls = _declared()
+    for name, args in decls.items():
+        res, argtypes = _lib.SIGNATURES[name]
+        assert len(argtypes) == len(args), name
+        for a, t in zip(args, argtypes):
+            if "*" in a or "rt_stream_t" in a:
+                assert t is ctypes.c_void_p or t is ctypes.c_char_p, (name, a)
+            elif a.startswith("int64_t"):
+                assert t is ctypes.c_int64, (name, a)
+            elif a.startswith("size_t"):
+                assert t is ctypes.c_size_t, (name, a)
+            elif a.startswith("double"):
+                assert t is ctypes.c_double, (name, a)
+            elif a.startswith("float"):
+                assert t is ctypes.c_float, (name, a)
+            elif a.startswith("int"):
+                assert t is ctypes.c_int, (name, a)
+
+
+def test_status_strings():
+    assert _lib.status_string(0) == "ok"
+    assert "wait" in _lib.status_string(_lib.RT_DEV_WAIT_TIMEOUT)
+    with pytest.raises(RuntimeError):
+        _lib.check(_lib.RT_ERR_INVALID_ARGUMENT, "x")
+
+
+def test_host_argument_checks_need_no_gpu():
+    lib = _lib.load()
+    # negative sizes and keep > window are rejected before any launch
+    assert lib.rt_kv_compact(None, None, 1, 0, 1, 0, 0, 256, 0, 4, None, 5, None, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_tree_attn(None, 0, 0, None, None, 0, 0, 0, None, 0, 0, None, 1, 1, 0, None, 32, 8, 128, 1.0,
+                            0, 0, None, 0, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_draft_topk(None, 0, 10, 1, 10, 2000, None, None, None, None, 0, None) == _lib.RT_ERR_UNSUPPORTED
+    assert lib.rt_tree_build(None, None, 15, 16, 2000, 0, None, 0, None, 0, 2, 0.0, 8, 1, 1, None, 6.0, None, 0,
+                             None, None, None, None, 1, None, None, None, 0, None, 0, None, None, None) in (
+        _lib.RT_ERR_UNSUPPORTED, _lib.RT_ERR_INVALID_ARGUMENT)
+
+
+def test_wrappers_refuse_cpu_tensors():
+    x = torch.zeros(4, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kernels.draft_topk(x, 2)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kernels.kv_compact(torch.zeros(1, 2, 5, 4), 1, torch.zeros(2, dtype=torch.long))
