@@ -172,8 +172,8 @@ int rt_draft_topk(const void* logits, int dtype, int64_t ld, int rows, int vocab
  * non-NULL; the last min(length, ctx_window) ids form the window
  * (ddtree.py:135-136).
  * log1p_table (binary64, DEVICE): log1p(c) for c = 0..table_len-1,
- * table_len > window length.  order_weight[n-2] = longer_weight**(n-2) for
- * n = 2..max_n.  Outputs (DEVICE): node_tokens[budget], node_depths[budget]
+ * table_len > window length.  order_weight (HOST array of max_n-1 doubles):
+ * order_weight[n-2] = longer_weight**(n-2) for n = 2..max_n.  Outputs (DEVICE): node_tokens[budget], node_depths[budget]
  * (int64), parents[budget+1] (int32, parents[0] = -1), mask
  * [(budget+1) x mask_words] ancestor bits, count (int32, nodes emitted).
  * When verify_ids / verify_pos are non-NULL they receive

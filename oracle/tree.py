@@ -103,12 +103,15 @@ def topk_logz(logits: np.ndarray, k: int):
         ids[r] = order[:k]
     top = np.take_along_axis(x, ids, axis=1)
     x64 = x.astype(np.float64)
-    m = x64.max(axis=1)
+    has_nan = np.isnan(x64).any(axis=1)
+    m = np.where(has_nan, np.nan, np.nanmax(np.where(np.isnan(x64), -np.inf, x64), axis=1))
     with np.errstate(invalid="ignore", over="ignore"):
         lse = m + np.log(np.exp(x64 - m[:, None]).sum(axis=1))
-    lse = np.where(np.isneginf(m), -np.inf, lse)
+    # torch.logsumexp: +inf if any +inf (and no NaN), -inf if all -inf, NaN if any NaN
+    lse = np.where(np.isinf(m), m, lse)
     log_z = lse.astype(np.float32)
-    top_logp = (top - log_z[:, None]).astype(np.float32)
+    with np.errstate(invalid="ignore"):
+        top_logp = (top - log_z[:, None]).astype(np.float32)
     return top_logp, ids, log_z, top
 
 

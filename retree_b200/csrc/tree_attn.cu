@@ -25,6 +25,7 @@
 //
 // Splits are merged by attn_combine_kernel (one warp per output row).
 #include <cuda.h>
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "host_util.h"
@@ -34,15 +35,18 @@ namespace rt {
 constexpr int kHD = 128;
 constexpr int kBM = 128;
 constexpr int kBN = 128;
-constexpr int kAttnThreads = 192;
+constexpr int kSoftmaxThreads = 256;  // warps 0-7: two threads per tile row
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
+constexpr int kAttnThreads = 320;
 constexpr uint32_t kTile = 128 * 128 * 2;  // one 128x128 bf16 tile
 constexpr uint32_t kHalf = kTile / 2;      // one 128-row x 64-column SW128 box
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kTile;
-constexpr uint32_t kOffV = 3 * kTile;
-constexpr uint32_t kOffP = 5 * kTile;
-constexpr uint32_t kOffBar = 6 * kTile;
-constexpr uint32_t kAttnSmem = kOffBar + 256 + 1024;  // + barriers + alignment slack
+constexpr uint32_t kOffK = kTile;           // 2 stages
+constexpr uint32_t kOffV = 3 * kTile;       // 2 stages
+constexpr uint32_t kOffP = 5 * kTile;       // 2 buffers
+constexpr uint32_t kOffBar = 7 * kTile;
+constexpr uint32_t kAttnSmem = kOffBar + 1536 + 1024;  // + barriers/exchange + alignment slack
 constexpr uint32_t kTmemCols = 512;                   // S0 | S1 | O | spare
 constexpr float kRescaleThreshold = 8.0f;             // log2 units
 
@@ -68,9 +72,10 @@ struct AttnParams {
 };
 
 struct Barriers {
-  uint64_t full_k[2], full_v[2], empty[2], s_full[2], s_free[2], p_full, o_done, fin;
+  uint64_t full_q, full_k[2], full_v[2], empty_k[2], empty_v[2], s_full[2], s_free[2], p_full[2], o_done[2], fin;
   uint32_t tmem_base;
   int abort_flag;
+  float xchg[2][kBM];  // per-row partial max / sum of the two column halves
 };
 
 __device__ __forceinline__ int64_t key_count(const AttnParams& p) {
@@ -94,12 +99,53 @@ __device__ __forceinline__ void write_neutral_partial(const AttnParams& p, int s
   }
 }
 
+// Raw S -> running max with four independent accumulators.
+__device__ __forceinline__ float max128(const uint32_t (&s)[4][32]) {
+  float a[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int c4 = 0; c4 < 4; ++c4)
+#pragma unroll
+    for (int c = 0; c < 32; ++c) a[c & 3] = fmaxf(a[c & 3], __uint_as_float(s[c4][c]));
+  return fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
+}
+
+// Visibility of the 32 keys [k0, k0+32) for one node: prefix keys (< L) are
+// visible, tree key t = key - L uses bit t of the node's mask row, keys at or
+// past L + n are hidden.
+__device__ __forceinline__ uint32_t visible_word(int64_t k0, int64_t L, int n, const uint32_t* mrow, int words) {
+  const int64_t pre = L - k0;  // prefix columns at the start of the window
+  if (pre >= 32) return 0xFFFFFFFFu;
+  uint32_t bits = pre > 0 ? ((1u << pre) - 1u) : 0u;
+  const int64_t t0 = k0 - L;  // tree index of column 0 (negative: starts in the prefix)
+  uint32_t tb;
+  if (t0 >= 0) {
+    const int w = static_cast<int>(t0 >> 5), sh = static_cast<int>(t0 & 31);
+    const uint32_t lo = w < words ? mrow[w] : 0u;
+    const uint32_t hi = (sh != 0 && w + 1 < words) ? mrow[w + 1] : 0u;
+    tb = sh ? ((lo >> sh) | (hi << (32 - sh))) : lo;
+  } else {
+    tb = mrow[0] << static_cast<int>(-t0);
+  }
+  // tree columns past the last node are hidden
+  const int64_t lim = static_cast<int64_t>(n) - t0;  // columns c < lim have t < n
+  if (lim < 32) tb &= lim <= 0 ? 0u : ((1u << lim) - 1u);
+  return bits | tb;
+}
+
+__device__ __forceinline__ uint32_t ex2_f16x2(float lo, float hi) {
+  uint32_t h, e;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
+  return e;
+}
+
 __global__ void __launch_bounds__(kAttnThreads, 1)
     tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
-                        const AttnParams p) {
+                        const __grid_constant__ CUtensorMap tmap_q, const AttnParams p, const int q_tma) {
   extern __shared__ unsigned char smem_raw[];
   // 1024-byte alignment for the SW128 atoms
-  unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers& bar = *reinterpret_cast<Barriers*>(smem + kOffBar);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, mt = blockIdx.z;
@@ -118,81 +164,109 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 
   if (tid == 0) {
+    mbar_init(&bar.full_q, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar.full_k[i], 1);
       mbar_init(&bar.full_v[i], 1);
-      mbar_init(&bar.empty[i], 1);
+      mbar_init(&bar.empty_k[i], 1);
+      mbar_init(&bar.empty_v[i], 1);
       mbar_init(&bar.s_full[i], 1);
-      mbar_init(&bar.s_free[i], 128);
+      mbar_init(&bar.s_free[i], kSoftmaxThreads);
+      mbar_init(&bar.p_full[i], kSoftmaxThreads);
+      mbar_init(&bar.o_done[i], 1);
     }
-    mbar_init(&bar.p_full, 128);
-    mbar_init(&bar.o_done, 1);
     mbar_init(&bar.fin, 1);
     bar.abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&bar.tmem_base, kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) {
-    prefetch_tmap(&tmap_k);
-    prefetch_tmap(&tmap_v);
-  }
-  // Q tile -> SW128 K-major smem (two 64-column boxes), zero rows past the tree
-  for (int c = tid; c < kBM * 16; c += kAttnThreads) {
-    const int r = c >> 4, ch = c & 15;
-    const int R = row0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (R < rows_total) {
-      const int node = R / G, h = kvh * G + (R - node * G);
-      v = *reinterpret_cast<const uint4*>(p.q + node * p.q_tok_stride + h * p.q_head_stride + ch * 16);
+  if (!q_tma) {
+    // Q tile -> SW128 K-major smem by plain loads (group sizes that do not tile 128 rows)
+    constexpr int kPer = (kBM * 16 + kAttnThreads - 1) / kAttnThreads;
+    uint4 v[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = tid + i * kAttnThreads;
+      const int r = c >> 4, ch = c & 15, R = row0 + r;
+      v[i] = make_uint4(0, 0, 0, 0);
+      if (c < kBM * 16 && R < rows_total) {
+        const int node = R / G, h = kvh * G + (R - node * G);
+        v[i] = *reinterpret_cast<const uint4*>(p.q + node * p.q_tok_stride + h * p.q_head_stride + ch * 16);
+      }
     }
-    const uint32_t off = kOffQ + (ch >> 3) * kHalf + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
-    *reinterpret_cast<uint4*>(smem + off) = v;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = tid + i * kAttnThreads;
+      if (c < kBM * 16) {
+        const int r = c >> 4, ch = c & 15;
+        const uint32_t off = kOffQ + (ch >> 3) * kHalf + r * 128 + (((ch & 7) ^ (r & 7)) << 4);
+        *reinterpret_cast<uint4*>(smem + off) = v[i];
+      }
+    }
+    fence_proxy_async_smem();
   }
-  fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = bar.tmem_base;
   volatile int* abort_flag = &bar.abort_flag;
 
-  if (warp == 4) {
-    // ---------------- TMA producer ----------------
+  if (warp == kProducerWarp) {
+    // ---------------- TMA producer: lane 0 Q and K, lane 1 V ----------------
     if (lane == 0) {
+      if (q_tma) {
+        prefetch_tmap(&tmap_q);
+        mbar_arrive_expect_tx(&bar.full_q, kTile);
+        const int tok0 = mt * (kBM / G);
+        tma_load_3d(smem + kOffQ, &tmap_q, &bar.full_q, 0, kvh * G, tok0);
+        tma_load_3d(smem + kOffQ + kHalf, &tmap_q, &bar.full_q, 64, kvh * G, tok0);
+      } else {
+        mbar_arrive(&bar.full_q);
+      }
       int issued = 0;
       for (int j = 0; j < nb; ++j) {
         const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&bar.empty[st], ph ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
+        // stage st is free once S(j-2) has consumed it
+        if (!mbar_wait(&bar.empty_k[st], ((j >> 1) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
         const int key0 = static_cast<int>((b0 + j) * kBN);
         unsigned char* kd = smem + kOffK + st * kTile;
-        unsigned char* vd = smem + kOffV + st * kTile;
         mbar_arrive_expect_tx(&bar.full_k[st], kTile);
         tma_load_3d(kd, &tmap_k, &bar.full_k[st], 0, key0, kvh);
         tma_load_3d(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh);
+        issued = j + 1;
+      }
+      if (*abort_flag) {
+        mbar_wait(&bar.full_q, 0, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+        for (int j = max(0, issued - 2); j < issued; ++j)
+          mbar_wait(&bar.full_k[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+      }
+    } else if (lane == 1) {
+      int issued = 0;
+      for (int j = 0; j < nb; ++j) {
+        const int st = j & 1;
+        // stage st is free once PV(j-2) has consumed it
+        if (!mbar_wait(&bar.empty_v[st], ((j >> 1) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
+        const int key0 = static_cast<int>((b0 + j) * kBN);
+        unsigned char* vd = smem + kOffV + st * kTile;
         mbar_arrive_expect_tx(&bar.full_v[st], kTile);
         tma_load_3d(vd, &tmap_v, &bar.full_v[st], 0, key0, kvh);
         tma_load_3d(vd + kHalf, &tmap_v, &bar.full_v[st], 64, key0, kvh);
         issued = j + 1;
       }
-      if (*abort_flag) {
-        // drain loads still in flight before the CTA exits
-        for (int j = max(0, issued - 2); j < issued; ++j) {
-          mbar_wait(&bar.full_k[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+      if (*abort_flag)
+        for (int j = max(0, issued - 2); j < issued; ++j)
           mbar_wait(&bar.full_v[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
-        }
-      }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false, false);
       constexpr uint32_t idesc_pv = idesc_bf16_f32(kBM, kHD, false, true);
       const uint32_t sq = smem_u32(smem + kOffQ);
-      const uint32_t sp = smem_u32(smem + kOffP);
-      bool ok = true;
+      bool ok = mbar_wait(&bar.full_q, 0, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
       for (int j = 0; j <= nb && ok; ++j) {
         if (j < nb) {
           const int st = j & 1, b = j & 1;
@@ -209,14 +283,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                      idesc_qk, kk > 0);
           }
           umma_commit(&bar.s_full[b]);
+          umma_commit(&bar.empty_k[st]);
         }
         if (j >= 1) {
-          const int jp = j - 1, stp = jp & 1;
-          ok = mbar_wait(&bar.p_full, jp & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT) &&
-               mbar_wait(&bar.full_v[stp], (jp >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+          const int jp = j - 1, pb = jp & 1;
+          const uint32_t pph = (jp >> 1) & 1;
+          ok = mbar_wait(&bar.p_full[pb], pph, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT) &&
+               mbar_wait(&bar.full_v[pb], pph, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t sv = smem_u32(smem + kOffV + stp * kTile);
+          const uint32_t sp = smem_u32(smem + kOffP + pb * kTile);
+          const uint32_t sv = smem_u32(smem + kOffV + pb * kTile);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
             const uint32_t poff = (kk >> 2) * kHalf + (kk & 3) * 32;
@@ -225,8 +302,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             umma_f16(tmem + 2 * kBN, smem_desc_sw128(sp + poff, 16, 1024),
                      smem_desc_sw128(sv + kk * 2048, kHalf, 1024), idesc_pv, (jp > 0 || kk > 0) ? 1u : 0u);
           }
-          umma_commit(&bar.o_done);
-          umma_commit(&bar.empty[stp]);
+          umma_commit(&bar.o_done[pb]);
+          umma_commit(&bar.empty_v[pb]);
         }
       }
       // all issued MMAs complete before TMEM is released
@@ -234,124 +311,151 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       mbar_wait(&bar.fin, 0, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
     }
   } else {
-    // ---------------- softmax / epilogue (warps 0-3) ----------------
-    const int r = tid;  // TMEM lane == tile row
+    // ---------------- softmax / epilogue (warps 0-7) ----------------
+    // Warp w reads TMEM lanes 32*(w%4)..+31 (its sub-partition) and owns key /
+    // head-dim columns [64*half, 64*half + 64) with half = w / 4, so every tile
+    // row is handled by two threads that exchange their partial max and sum.
+    const int half = warp >> 2;
+    const int r = tid & (kBM - 1);  // TMEM lane == tile row
     const int R = row0 + r;
     const bool valid = R < rows_total;
+    const bool warp_live = row0 + (warp & 3) * 32 < rows_total;  // some row of this warp is a real query
     const int node = valid ? R / G : 0;
-    const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t col0 = half * 64;  // this thread's S / O columns
     const uint32_t* mrow = p.mask + static_cast<int64_t>(node) * p.mask_words;
-    float m = -INFINITY, l = 0.f;
+    const float sl2 = p.scale_log2;
+    float m = -INFINITY, l = 0.f;  // m in scaled log2 units; l = this half's partial sum
     bool ok = true;
-    uint32_t sreg[4][32];
+    uint32_t sreg[2][32];
+    // Every softmax thread passes both named barriers of every block, whatever
+    // happens to its waits: after a time-out `ok` turns false (warp-uniformly)
+    // and the thread only keeps the barrier count, so no thread is left waiting.
     for (int j = 0; j < nb; ++j) {
       const int b = j & 1;
-      ok = mbar_wait(&bar.s_full[b], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
-      if (!ok) break;
-      tc_fence_after();
-#pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) tmem_ld32(tmem + lane_base + b * kBN + c4 * 32, sreg[c4]);
-      tmem_wait_ld();
-      tc_fence_before();
-      mbar_arrive(&bar.s_free[b]);
-      const int64_t key0 = (b0 + j) * kBN;
+      const uint32_t ph = (j >> 1) & 1;
+      if (ok) ok = mbar_wait(&bar.s_full[b], ph, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+      ok = __all_sync(0xFFFFFFFFu, ok);
+      const bool work = ok && warp_live;
       float mloc = -INFINITY;
-      if (valid && key0 + kBN <= L) {
+      if (work) {
+        tc_fence_after();
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4)
+        for (int c2 = 0; c2 < 2; ++c2) tmem_ld32(tmem + lane_base + b * kBN + col0 + c2 * 32, sreg[c2]);
+        tmem_wait_ld();
+        tc_fence_before();
+      }
+      mbar_arrive(&bar.s_free[b]);
+      if (work) {
+        const int64_t key0 = (b0 + j) * kBN + col0;
+        if (!valid || key0 + 64 > L) {
+          // columns reach the tree keys (or the end): hide per a 32-bit visibility word
 #pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const float x = __uint_as_float(sreg[c4][c]) * p.scale_log2;
-            sreg[c4][c] = __float_as_uint(x);
-            mloc = fmaxf(mloc, x);
-          }
-      } else {
-        // block reaches the tree keys (or the end): visibility per column
+          for (int c2 = 0; c2 < 2; ++c2) {
+            const uint32_t vm = valid ? visible_word(key0 + c2 * 32, L, p.n, mrow, p.mask_words) : 0u;
+            if (vm != 0xFFFFFFFFu) {
 #pragma unroll
-        for (int c4 = 0; c4 < 4; ++c4) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            const int64_t key = key0 + c4 * 32 + c;
-            bool vis = false;
-            if (valid) {
-              if (key < L) {
-                vis = true;
-              } else if (key < total_keys) {
-                const int64_t t = key - L;
-                vis = (mrow[t >> 5] >> (t & 31)) & 1u;
-              }
+              for (int c = 0; c < 32; ++c)
+                if (!((vm >> c) & 1u)) sreg[c2][c] = __float_as_uint(-INFINITY);
             }
-            const float x = vis ? __uint_as_float(sreg[c4][c]) * p.scale_log2 : -INFINITY;
-            sreg[c4][c] = __float_as_uint(x);
-            mloc = fmaxf(mloc, x);
           }
         }
+        float a[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2)
+#pragma unroll
+          for (int c = 0; c < 32; ++c) a[c & 3] = fmaxf(a[c & 3], __uint_as_float(sreg[c2][c]));
+        mloc = fmaxf(fmaxf(a[0], a[1]), fmaxf(a[2], a[3]));
       }
-      const float m_new = fmaxf(m, mloc);
-      const bool need = m_new > m + kRescaleThreshold;  // false while both are -inf
-      if (j > 0) {
-        ok = mbar_wait(&bar.o_done, (j - 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(0xFFFFFFFFu, need)) {
+      // row max over both halves (named barrier among the 256 softmax threads)
+      bar.xchg[half][r] = mloc;
+      asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxThreads) : "memory");
+      const float mrow_max = fmaxf(bar.xchg[0][r], bar.xchg[1][r]);
+      asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxThreads) : "memory");
+      if (!work) {
+        mbar_arrive(&bar.p_full[b]);
+        continue;
+      }
+      const float m_new = fmaxf(m, mrow_max * sl2);
+      const bool need = m_new > m + kRescaleThreshold;  // identical in both halves; false while -inf
+      if (__any_sync(0xFFFFFFFFu, need) && j > 0) {
+        // O must hold blocks <= j-1 before it is rescaled
+        ok = mbar_wait(&bar.o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+        ok = __all_sync(0xFFFFFFFFu, ok);
+        if (ok) {
+          tc_fence_after();
           const float f = need ? ex2(m - m_new) : 1.f;  // ex2(-inf) = 0 when m was -inf
           uint32_t o[32];
 #pragma unroll
-          for (int c4 = 0; c4 < 4; ++c4) {
-            tmem_ld32(tmem + lane_base + 2 * kBN + c4 * 32, o);
+          for (int c2 = 0; c2 < 2; ++c2) {
+            tmem_ld32(tmem + lane_base + 2 * kBN + col0 + c2 * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < 32; ++c) o[c] = __float_as_uint(__uint_as_float(o[c]) * f);
-            tmem_st32(tmem + lane_base + 2 * kBN + c4 * 32, o);
+            tmem_st32(tmem + lane_base + 2 * kBN + col0 + c2 * 32, o);
           }
           tmem_wait_st();
-          if (need) l *= f;
+          l *= f;
         }
       }
       if (need) m = m_new;
       const float mu = (m == -INFINITY) ? 0.f : m;
-      // P = exp2(s - m) as bf16, SW128 K-major (keys 0-63 | 64-127)
-      float lsum = 0.f;
+      if (ok && j >= 2) {
+        // P buffer b was last read by PV(j-2)
+        ok = mbar_wait(&bar.o_done[b], ((j - 2) >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+      }
+      if (!ok) {
+        mbar_arrive(&bar.p_full[b]);
+        continue;
+      }
+      // P = exp2(s*scale - m): exp2 on packed f16 pairs, sum in fp32, stored as
+      // bf16 in this half's SW128 K-major box of the P tile
+      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      unsigned char* pbuf = smem + kOffP + b * kTile + half * kHalf;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < 2; ++c2) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {  // 8 keys = one 16-byte chunk
-          float e[8];
+          uint32_t pk[4];
 #pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            e[t] = ex2(__uint_as_float(sreg[c4][q * 8 + t]) - mu);
-            lsum += e[t];
+          for (int t = 0; t < 4; ++t) {
+            const float x0 = fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t]), sl2, -mu);
+            const float x1 = fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t + 1]), sl2, -mu);
+            const uint32_t e = ex2_f16x2(x0, x1);
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e));
+            ls[t] += f.x + f.y;
+            pk[t] = pack_bf16x2(f.x, f.y);
           }
-          const int col = c4 * 32 + q * 8;
-          const int ch = (col & 63) >> 3;
-          const uint32_t off = kOffP + (col >> 6) * kHalf + r * 128 + ((ch ^ (r & 7)) << 4);
-          uint4 pk;
-          pk.x = pack_bf16x2(e[0], e[1]);
-          pk.y = pack_bf16x2(e[2], e[3]);
-          pk.z = pack_bf16x2(e[4], e[5]);
-          pk.w = pack_bf16x2(e[6], e[7]);
-          *reinterpret_cast<uint4*>(smem + off) = pk;
+          const int ch = c2 * 4 + q;  // 16-byte chunk within the 128-byte row
+          const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
+          *reinterpret_cast<uint4*>(pbuf + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
-      l += lsum;
+      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(&bar.p_full);
+      mbar_arrive(&bar.p_full[b]);
     }
-    if (ok) ok = mbar_wait(&bar.o_done, (nb - 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
-    if (ok) {
+    // full row sum = both halves
+    if (ok) ok = mbar_wait(&bar.o_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+    ok = __all_sync(0xFFFFFFFFu, ok);
+    bar.xchg[half][r] = l;
+    asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxThreads) : "memory");
+    const float lrow = bar.xchg[0][r] + bar.xchg[1][r];
+    if (ok && warp_live) {
       tc_fence_after();
       const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
       const int h = valid ? kvh * G + (R - node * G) : 0;
 #pragma unroll
-      for (int c4 = 0; c4 < 4; ++c4) {
+      for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t o[32];
-        tmem_ld32(tmem + lane_base + 2 * kBN + c4 * 32, o);
+        tmem_ld32(tmem + lane_base + 2 * kBN + col0 + c2 * 32, o);
         tmem_wait_ld();
         if (!valid) continue;
+        const int d0 = col0 + c2 * 32;  // head-dim offset of these 32 values
         if (p.num_splits == 1) {
-          const float inv = 1.f / l;
-          char* dst = p.out + node * p.out_tok_stride + h * p.out_head_stride + c4 * 64;
+          const float inv = 1.f / lrow;
+          char* dst = p.out + node * p.out_tok_stride + h * p.out_head_stride + d0 * 2;
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             uint4 pk;
@@ -362,7 +466,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             *reinterpret_cast<uint4*>(dst + q * 16) = pk;
           }
         } else {
-          float* dst = p.ws_o + ((static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + R) * kHD + c4 * 32;
+          float* dst = p.ws_o + ((static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + R) * kHD + d0;
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             *reinterpret_cast<float4*>(dst + q * 4) =
@@ -370,13 +474,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                             __uint_as_float(o[q * 4 + 3]));
         }
       }
-      if (valid && p.num_splits > 1)
-        p.ws_ml[(static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + R] = make_float2(m, l);
+      if (valid && half == 0 && p.num_splits > 1)
+        p.ws_ml[(static_cast<int64_t>(split) * p.num_kv_heads + kvh) * rows_ws + R] = make_float2(m, lrow);
     }
     tc_fence_before();
   }
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
@@ -580,6 +684,22 @@ static int make_kv_tmap(CUtensorMap* m, const void* base, int64_t head_stride, i
   return r == CUDA_SUCCESS ? RT_OK : RT_ERR_INVALID_ARGUMENT;
 }
 
+// Q viewed as [n tokens][Hq heads][128] (any token / head strides): one box is
+// 128/G tokens x G heads x 64 dims, i.e. the 128 tile rows in (node, head) order.
+static int make_q_tmap(CUtensorMap* m, const void* q, int64_t tok_stride, int64_t head_stride, int n, int hq,
+                       int G) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return RT_ERR_CUDA;
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(hq), static_cast<cuuint64_t>(n)};
+  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(head_stride), static_cast<cuuint64_t>(tok_stride)};
+  const cuuint32_t box[3] = {64, static_cast<cuuint32_t>(G), static_cast<cuuint32_t>(kBM / G)};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? RT_OK : RT_ERR_INVALID_ARGUMENT;
+}
+
 static int tiles_for(int n, int G) { return (n * G + kBM - 1) / kBM; }
 
 static int default_splits(int n, int G, int hkv, int64_t prefix_len, bool tc) {
@@ -588,7 +708,8 @@ static int default_splits(int n, int G, int hkv, int64_t prefix_len, bool tc) {
   const int64_t nblk = (keys + blk - 1) / blk;
   const int tiles = tc ? tiles_for(n, G) : 1;
   const int64_t ctas = static_cast<int64_t>(hkv) * tiles;
-  const int64_t target = std::min<int64_t>(256, (148 + ctas - 1) / ctas);  // about one CTA per SM
+  // one wave: at most one CTA per SM (the tcgen05 kernel holds a whole SM)
+  const int64_t target = std::min<int64_t>(256, std::max<int64_t>(1, 148 / ctas));
   const int64_t per = std::max<int64_t>(1, (nblk + target - 1) / target);    // blocks per split
   return static_cast<int>(std::max<int64_t>(1, (nblk + per - 1) / per));
 }
@@ -677,9 +798,15 @@ extern "C" int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_
     if (rc != RT_OK) return rc;
     rc = make_kv_tmap(&tv, v, kv_head_stride, kv_row_stride, kv_capacity, num_kv_heads);
     if (rc != RT_OK) return rc;
+    CUtensorMap tq = tk;
+    int q_tma = (kBM % G == 0 && q_tok_stride > 0 && q_head_stride > 0) ? 1 : 0;
+    if (q_tma && make_q_tmap(&tq, q, q_tok_stride, q_head_stride, n, num_q_heads, G) != RT_OK) {
+      tq = tk;
+      q_tma = 0;
+    }
     set_smem_limit(tree_attn_tc_kernel, kAttnSmem);
     const dim3 grid(num_splits, num_kv_heads, p.tiles);
-    tree_attn_tc_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(tk, tv, p);
+    tree_attn_tc_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(tk, tv, tq, p, q_tma);
   } else {
     const dim3 grid(num_splits, num_kv_heads);
     tree_attn_simt_kernel<<<grid, 128, 0, s>>>(p);

@@ -7,6 +7,7 @@ is no CPU path, and a missing library raises (``retree_b200._lib.load``).
 
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import numpy as np
@@ -278,8 +279,8 @@ def tree_build(top_logp: torch.Tensor, top_ids: torch.Tensor, budget: int, strat
             verify_pos=torch.empty(budget + 1, dtype=torch.int64, device=dev),
         )
     max_n = int(params.max_n) if code else 2
-    ow = torch.tensor([float(params.longer_weight ** max(0, n - 2)) for n in range(2, max_n + 1)],
-                      dtype=torch.float64, device=dev)
+    ow_vals = [float(params.longer_weight ** max(0, n - 2)) for n in range(2, max_n + 1)]
+    ow = (ctypes.c_double * max(len(ow_vals), 1))(*ow_vals)
     window = int(params.context_window)
     if ctx is not None:
         clen = int(ctx.numel()) if ctx_len is None else int(ctx_len)
@@ -291,7 +292,7 @@ def tree_build(top_logp: torch.Tensor, top_ids: torch.Tensor, budget: int, strat
     rc = lib.rt_tree_build(
         top_logp.data_ptr(), top_ids.data_ptr(), rows, k, int(budget), code, _ptr(ctx), clen, _ptr(ctx_len_dev),
         window, max_n, float(params.beta), int(params.rank_cap), int(params.min_count), int(bool(params.use_log_count)),
-        ow.data_ptr(), float(params.max_token_bonus), table.data_ptr(), int(table.numel()),
+        ctypes.addressof(ow), float(params.max_token_bonus), table.data_ptr(), int(table.numel()),
         out["tokens"].data_ptr(), out["depths"].data_ptr(), out["parents"].data_ptr(), out["mask"].data_ptr(), w,
         out["count"].data_ptr(), _ptr(out.get("verify_ids")), _ptr(out.get("verify_pos")), int(root), _ptr(root_dev),
         int(start), _ptr(start_dev), _STATE.status(dev).data_ptr(), _stream(dev))

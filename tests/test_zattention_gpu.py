@@ -50,7 +50,7 @@ def test_attention_cfg1_against_reference_sdpa_output():
     v = torch.randn((1, 8, past + n, 128), generator=g)
     vis = ot.visibility(t["parents"])
     qb, kb, vb = (x.to(torch.bfloat16) for x in (q, k, v))
-    for path in (1, 2):
+    for path in ((1, 2) if n * 4 <= 64 else (1,)):
         out = kernels.tree_attention(qb.to(dev), kb.to(dev), vb.to(dev), bits_tensor(vis, dev), past, path=path)
         kernels.check_device_status(dev)
         _check(out, qb, kb[0], vb[0], past, vis)
