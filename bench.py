@@ -1,0 +1,351 @@
+#!/usr/bin/env python
+"""Verify-round throughput of the B200 tree-verification path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one ReTree/DDTree verify round on every rank: draft top-k and
+rank-gated n-gram tree build from that round's draft logits, the target
+forward over the 1+budget tree nodes with tree-verify attention and in-place
+cache append, argmax posterior, exact walk + commit, and KV compaction.
+The draft model forward is not part of the round (the reference times it as a
+separate stage); seeded synthetic draft logits (N(0,1) + Zipf boost, bf16 as
+an lm_head emits them) stand in for it.  Default workload: random-init
+Qwen3-4B (bf16, 36 layers), 2048-token uniform random prompt, draft block 16,
+tree budget 16.  With N>1 ranks (torchrun) every rank verifies its own
+request (data parallel, as the reference's benchmark shards requests) and the
+ranks all-gather a fixed-shape recovery-memory delta after every step.
+
+Prints ONE JSON line (rank 0).  ``value`` = verify rounds/s over all ranks with
+inputs resident on the device; ``e2e`` = the same through the public API with
+the draft logits copied from pinned host memory and the committed tokens read
+back every round; ``roofline`` = the tree-verify attention kernel measured
+live on the timed rounds; ``cpu_baseline`` = the reference's round on the host
+cores (a bounded sample).  ``--impl reference`` times that CPU round alone.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    # name: model geometry, prompt length, tree budget, draft block
+    "qwen3-4b-b16": dict(model="qwen3-4b", prompt=2048, budget=16, block=16),
+    "qwen3-4b-b64": dict(model="qwen3-4b", prompt=2048, budget=64, block=16),
+    "qwen3-8b-b64": dict(model="qwen3-8b", prompt=4096, budget=64, block=16),
+}
+DELTA_PAIRS = 4096  # recovery-memory delta exchanged per step at N>1 (int32 draft, target, count)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=24)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3-4b-b16")
+    ap.add_argument("--strategy", default="rank_gated_ngram")
+    ap.add_argument("--cpu-sample-rounds", type=int, default=3)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def draft_logits_np(seed: int, block: int, vocab: int) -> np.ndarray:
+    from retree_b200 import synthetic
+    return synthetic.draft_logits(seed, block, vocab)[-(block - 1):]
+
+
+def measured_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def profile_traffic(workload: str):
+    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+    path = os.path.join(ROOT, "profiles", "tree_attn_ncu.md")
+    if not os.path.exists(path):
+        return None
+    m = re.search(rf"traffic_bytes_per_launch\[{re.escape(workload)}\]:\s*([0-9.eE+]+)", open(path).read())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    def __init__(self, index: int):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            ids = [x.strip() for x in vis.split(",") if x.strip()]
+            if index < len(ids) and ids[index].isdigit():
+                index = int(ids[index])
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+
+    def stop(self) -> dict:
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_round_sample(cfg, wl, rounds: int, strategy: str):
+    """The reference's verify round on the host cores; returns (rounds/s, seconds, cores)."""
+    from oracle.tree import NgramParams
+    from oracle.verify_round import CpuVerifyRound
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    r = CpuVerifyRound(cfg, wl["prompt"], wl["budget"], strategy=strategy, params=NgramParams())
+    drafts = [draft_logits_np(1000 + i, wl["block"], cfg.vocab_size) for i in range(rounds + 1)]
+    r.round(drafts[0])  # warm-up
+    t0 = time.perf_counter()
+    for i in range(rounds):
+        r.round(drafts[i + 1])
+    dt = time.perf_counter() - t0
+    return rounds / dt, dt, cores
+
+
+def run_reference(args, wl, rank, world):
+    if rank != 0:
+        return
+    from retree_b200.target import qwen3_config
+    cfg = qwen3_config(wl["model"])
+    from oracle.tree import NgramParams
+    from oracle.verify_round import CpuVerifyRound
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    r = CpuVerifyRound(cfg, wl["prompt"], wl["budget"], strategy=args.strategy, params=NgramParams())
+    drafts = [draft_logits_np(1000 + i, wl["block"], cfg.vocab_size) for i in range(args.warmup + args.steps)]
+    for i in range(args.warmup):
+        r.round(drafts[i])
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        r.round(drafts[args.warmup + i])
+    dt = time.perf_counter() - t0
+    value = args.steps / dt
+    sample = (f"{args.steps} verify rounds of the reference path on the host CPU (oracle restatement: tree build, "
+              f"dense-mask compile, HF sdpa forward bf16, walk, index_select compaction) over a random-KV prefix of "
+              f"{wl['prompt']} tokens")
+    print(json.dumps({
+        "impl": "reference", "metric": "verify rounds/sec", "value": value, "unit": "rounds/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "model": wl["model"], "prompt": wl["prompt"], "budget": wl["budget"],
+                   "draft_block": wl["block"], "strategy": args.strategy, "parallelism": "host CPU, rank 0 only"},
+        "cpu_baseline": {"value": value, "unit": "rounds/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "rounds/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def attn_bytes(L: int, n: int, hq: int, hkv: int, hd: int = 128) -> int:
+    """Algorithmic HBM bytes of one tree-attention launch: K+V prefix and tree rows, q in, out, mask."""
+    return (L + n) * 2 * hkv * hd * 2 + 2 * n * hq * hd * 2 + n * ((n + 31) // 32) * 4
+
+
+def run_ours(args, wl, rank, world, local_rank):
+    import torch.distributed as dist
+
+    from retree_b200 import attention, kernels
+    from retree_b200.target import build_target, qwen3_config
+    from retree_b200.verify import TreeVerifier
+
+    os.environ["DDTREE_TREE_STRATEGY"] = args.strategy
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    cfg = qwen3_config(wl["model"])
+    target = build_target(cfg, device=dev, seed=0)
+    steps, warm = args.steps, args.warmup
+    total_rounds = warm + steps
+    max_len = wl["prompt"] + total_rounds * (wl["block"] + 2) + 64
+    # draft logits for every round: bf16 as the lm_head emits them; pinned host copies for the e2e leg
+    host = [torch.from_numpy(draft_logits_np(1000 + 7919 * rank + i, wl["block"], cfg.vocab_size)).to(torch.bfloat16)
+            for i in range(total_rounds)]
+    pinned = [h.pin_memory() for h in host]
+    resident = [h.to(dev) for h in host]
+    prompt = torch.from_numpy(np.random.default_rng(rank).integers(0, cfg.vocab_size, size=wl["prompt"]))[None]
+
+    def fresh():
+        v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1)
+        v.prefill(prompt.to(dev))
+        return v
+
+    delta_send = torch.zeros((DELTA_PAIRS, 3), dtype=torch.int32, device=dev)
+    delta_recv = torch.zeros((world, DELTA_PAIRS, 3), dtype=torch.int32, device=dev) if world > 1 else None
+
+    def exchange():
+        if world > 1:
+            dist.all_gather_into_tensor(delta_recv.view(world * DELTA_PAIRS, 3), delta_send)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def timed(fn):
+        barrier()
+        t0 = time.perf_counter()
+        fn()
+        barrier()
+        dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+        return float(dt.item())
+
+    # ---- device-resident rounds (value) ----
+    v = fresh()
+    for i in range(warm):
+        v.round(resident[i])
+        exchange()
+    attention.PROFILE = []
+    kernels.LAUNCHES = 0
+    sampler = ClockSampler(dev.index) if rank == 0 else None
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    accepted = []
+
+    def rounds_resident():
+        ev0.record()
+        for i in range(steps):
+            accepted.append(v.round(resident[warm + i]))
+            exchange()
+        ev1.record()
+
+    wall = timed(rounds_resident)
+    clocks = sampler.stop() if sampler else None
+    launches = kernels.LAUNCHES
+    torch.cuda.synchronize()
+    dev_ms = torch.tensor([ev0.elapsed_time(ev1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(dev_ms, op=dist.ReduceOp.MAX)
+    dev_s = float(dev_ms.item()) / 1000.0
+    prof = attention.PROFILE
+    attention.PROFILE = None
+    attn_ms = [a.elapsed_time(b) for a, b, *_ in prof]
+    L_avg = sum(p[2] for p in prof) / len(prof)
+    n_tree = prof[0][3]
+    byts = sum(attn_bytes(p[2], p[3], p[4], p[5]) for p in prof) / len(prof)
+    attn_us = 1000.0 * sum(attn_ms) / len(attn_ms)
+
+    # ---- end to end through the public API: host draft logits in, committed tokens out ----
+    v2 = fresh()
+    out_host = torch.empty(wl["budget"] + 2, dtype=torch.int64).pin_memory()
+    for i in range(warm):
+        v2.round(pinned[i].to(dev, non_blocking=True))
+        exchange()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def rounds_e2e():
+        e0.record()
+        for i in range(steps):
+            logits = pinned[warm + i].to(dev, non_blocking=True)
+            s0 = v2.start
+            acc = v2.round(logits)
+            out_host[: acc + 1].copy_(v2.output_ids[s0: s0 + acc + 1])
+            exchange()
+        e1.record()
+
+    timed(rounds_e2e)
+    e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_s = float(e2e_ms.item()) / 1000.0
+    h2d = host[0].numel() * host[0].element_size()
+    d2h = 8 * (wl["budget"] + 2) + 4  # committed tokens + accepted count
+
+    if rank != 0:
+        return
+    hbm_peak, tf_peak, peak_kind = measured_peaks()
+    achieved = byts / (attn_us * 1e-6) / 1e9
+    traffic = profile_traffic(args.workload)
+    cpu = None
+    if not args.no_cpu_baseline:
+        del v, v2
+        torch.cuda.empty_cache()
+        rps, secs, cores = cpu_round_sample(cfg, wl, args.cpu_sample_rounds, args.strategy)
+        cpu = {"value": rps, "unit": "rounds/s", "cores": cores, "kind": "port",
+               "sample": (f"{args.cpu_sample_rounds} verify rounds ({secs:.1f} s) of the reference path on the host "
+                          f"CPU: oracle tree build, dense-mask compile, HF sdpa forward (bf16), walk, compaction, "
+                          f"random-KV prefix of {wl['prompt']} tokens")}
+    value = world * steps / dev_s
+    print(json.dumps({
+        "metric": "verify rounds/sec", "value": value, "unit": "rounds/s", "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": 1000.0 * dev_s / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded draft logits, uniform prompt, random-init "
+                                                      "weights)",
+        "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": wl["prompt"],
+                   "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
+                   "parallelism": f"dp{world} (one request per GPU)" + (
+                       ", recovery-delta all-gather per step" if world > 1 else ""),
+                   "l2": "inputs > L2 (8 GB of weights and the KV cache stream every round)",
+                   "mean_accepted": sum(accepted) / len(accepted), "wall_s": wall},
+        "roofline": {"kernel": "tree_attn (rt_tree_attn)", "bound": "hbm", "achieved": achieved, "peak": hbm_peak,
+                     "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": traffic,
+                     "peak_kind": peak_kind, "launches": len(prof), "avg_launch_us": attn_us,
+                     "algorithmic_bytes_per_launch": byts, "prefix_len_avg": L_avg, "tree_nodes": n_tree},
+        "cpu_baseline": cpu,
+        "e2e": {"value": world * steps / e2e_s, "unit": "rounds/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }), flush=True)
+
+
+def main():
+    args = parse()
+    wl = WORKLOADS[args.workload]
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    if args.impl == "reference":
+        run_reference(args, wl, rank, world)
+        return
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    try:
+        run_ours(args, wl, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

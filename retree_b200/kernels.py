@@ -60,6 +60,14 @@ class _DeviceState:
 
 _STATE = _DeviceState()
 
+#: number of kernel launches issued through these wrappers (for launch accounting)
+LAUNCHES = 0
+
+
+def _count(n: int = 1) -> None:
+    global LAUNCHES
+    LAUNCHES += n
+
 
 def status_tensor(device) -> torch.Tensor:
     """The device status word the kernels of this process report into."""
@@ -118,6 +126,7 @@ def kv_compact(tensors, past_length: int, keep: torch.Tensor, cur_length: int | 
                                v.shape[2] * es, int(past_length), cur, keep.data_ptr(), nk, _ptr(n_keep_dev),
                                _STATE.status(t.device).data_ptr(), _stream(t.device))
         _lib.check(rc, "rt_kv_compact")
+        _count()
 
 
 def kv_append(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor,
@@ -136,6 +145,7 @@ def kv_append(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.Tensor,
                           d * es, k_cache.shape[1], int(offset), _ptr(offset_dev),
                           _STATE.status(k_cache.device).data_ptr(), _stream(k_cache.device))
     _lib.check(rc, "rt_kv_append")
+    _count()
 
 
 def _as3(t: torch.Tensor) -> torch.Tensor:
@@ -193,6 +203,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
                           hq, hkv, d, scale, splits, path, _ptr(ws), ws_bytes,
                           _STATE.status(q.device).data_ptr(), _stream(q.device))
     _lib.check(rc, "rt_tree_attn")
+    _count(2 if splits > 1 else 1)
     return out
 
 
@@ -208,6 +219,7 @@ def mask_from_dense(dense: torch.Tensor, col0: int, n: int, words: int | None = 
     rc = lib.rt_mask_from_dense(d2.data_ptr(), _DTYPE_CODE[d2.dtype], d2.stride(0), int(col0), n, bits.data_ptr(),
                                 w, _stream(dense.device))
     _lib.check(rc, "rt_mask_from_dense")
+    _count()
     return bits
 
 
@@ -232,6 +244,7 @@ def draft_topk(logits: torch.Tensor, k: int, out=None):
                            out[0].data_ptr(), out[1].data_ptr(), out[2].data_ptr(), ws.data_ptr(), ws_bytes,
                            _stream(dev))
     _lib.check(rc, "rt_draft_topk")
+    _count(2)
     return out
 
 
@@ -286,8 +299,8 @@ def tree_build(top_logp: torch.Tensor, top_ids: torch.Tensor, budget: int, strat
         clen = int(ctx.numel()) if ctx_len is None else int(ctx_len)
     else:
         clen = 0
-    table_n = (window if window > 0 else max(clen, 1)) if ctx_len_dev is not None else \
-        (min(clen, window) if window > 0 else clen)
+    # one table per window size (not per context length), so it is uploaded once
+    table_n = window if window > 0 else max(clen, 1)
     table = log1p_table(dev, max(table_n, 1) + 1)
     rc = lib.rt_tree_build(
         top_logp.data_ptr(), top_ids.data_ptr(), rows, k, int(budget), code, _ptr(ctx), clen, _ptr(ctx_len_dev),
@@ -297,6 +310,7 @@ def tree_build(top_logp: torch.Tensor, top_ids: torch.Tensor, budget: int, strat
         out["count"].data_ptr(), _ptr(out.get("verify_ids")), _ptr(out.get("verify_pos")), int(root), _ptr(root_dev),
         int(start), _ptr(start_dev), _STATE.status(dev).data_ptr(), _stream(dev))
     _lib.check(rc, "rt_tree_build")
+    _count()
     out["_keep_alive"] = (ow, table)
     return out
 
@@ -322,6 +336,7 @@ def tree_walk(parents: torch.Tensor, tokens: torch.Tensor, posterior: torch.Tens
                           _ptr(verify_ids), _ptr(output_ids), 0 if output_ids is None else output_ids.numel(),
                           _ptr(start_dev), _STATE.status(dev).data_ptr(), _stream(dev))
     _lib.check(rc, "rt_tree_walk")
+    _count()
     return out
 
 

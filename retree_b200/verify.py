@@ -1,0 +1,259 @@
+"""Device-resident tree-verify rounds over a transformers causal LM.
+
+``TreeVerifier`` holds what the reference's decode loops keep between rounds
+(ddtree.py:765-795, retree.py:228-264): the output-id buffer, the target KV
+cache (a ``TreeKVCache`` here), the tree buffers, and the stage timers.  One
+``round(draft_logits)`` is the verification hot path:
+
+  1. draft top-k + best-first expansion   (kernels: rt_draft_topk, rt_tree_build)
+     -> node tokens / depths / parents, packed ancestor mask, verify ids and
+        positions, all on the device (no host copy of the draft logits);
+  2. one target forward over the 1+budget nodes (``retree_tree`` attention,
+     in-place cache append);
+  3. posterior = argmax (temperature 0) or multinomial sample;
+  4. exact walk + commit to the output ids (rt_tree_walk), or a host walk
+     callback (ReTree's sibling recovery);
+  5. compaction of the accepted rows of every layer in one launch
+     (rt_kv_compact) and the cache length update.
+
+The host reads back one small vector per round (accepted count, committed
+tokens) -- the reference syncs several times per round (ddtree.py:361-367,
+:653, :939-942).
+"""
+
+from __future__ import annotations
+
+import time
+from types import SimpleNamespace
+
+import torch
+
+from . import kernels
+from .attention import NAME as ATTN_NAME
+from .attention import attach
+from .cache import TreeKVCache
+from .ddtree import (DDTREE_STAGE_ORDER, DDTREE_TREE_BUILD_STAGE_ORDER, build_tree_device, cuda_time,
+                     empty_stage_times, resolve_strategy, sample)
+
+
+def expected_tree_size(budget: int, rows: int, vocab: int) -> int:
+    """Nodes the best-first expansion emits: ``budget`` unless the tree runs out of candidates."""
+    k = min(max(budget, 1), vocab)
+    total, level = 0, 1
+    for _ in range(rows):
+        level *= k
+        total += level
+        if total >= budget:
+            return budget
+    return min(budget, total)
+
+
+def extract_context_feature(hidden_states, layer_ids):
+    """Concatenate the selected target hidden states (model/utils.py:40-49)."""
+    return torch.cat([hidden_states[i + 1] for i in layer_ids], dim=-1)
+
+
+class TreeVerifier:
+    def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
+                 temperature: float = 0.0, target_layer_ids=None, device=None):
+        cfg = target.config
+        if getattr(cfg, "_attn_implementation", None) != ATTN_NAME:
+            raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
+        self.target = target
+        self.device = torch.device(device) if device is not None else next(target.parameters()).device
+        self.budget = max(int(tree_budget), 0)
+        self.horizon = int(draft_horizon)
+        self.temperature = float(temperature)
+        self.n_max = 1 + self.budget
+        self.words = (self.n_max + 31) // 32
+        self.max_length = int(max_length)
+        self.cache = TreeKVCache.for_model(cfg, capacity=self.max_length + self.n_max + 128, device=self.device)
+        self.output_ids = torch.zeros(self.max_length + self.n_max + 1, dtype=torch.long, device=self.device)
+        self.start_dev = torch.zeros(1, dtype=torch.int64, device=self.device)
+        self.start = 0
+        self.target_layer_ids = target_layer_ids
+        self.target_hidden = None
+        d = self.device
+        b = max(self.budget, 1)
+        self.tree = dict(
+            tokens=torch.zeros(b, dtype=torch.int64, device=d),
+            depths=torch.zeros(b, dtype=torch.int64, device=d),
+            parents=torch.zeros(self.n_max, dtype=torch.int32, device=d),
+            mask=torch.zeros((self.n_max, self.words), dtype=torch.int32, device=d),
+            count=torch.zeros(1, dtype=torch.int32, device=d),
+            verify_ids=torch.zeros(self.n_max, dtype=torch.int64, device=d),
+            verify_pos=torch.zeros(self.n_max, dtype=torch.int64, device=d),
+        )
+        self.walk = dict(accepted=torch.zeros(self.n_max, dtype=torch.int64, device=d),
+                         accepted_len=torch.zeros(1, dtype=torch.int32, device=d),
+                         next_token=torch.zeros(1, dtype=torch.int64, device=d))
+        self.stage_times = empty_stage_times(DDTREE_STAGE_ORDER + DDTREE_TREE_BUILD_STAGE_ORDER)
+        self.timed = False
+        self.debug = False  # keep the posterior and the pre-compaction cache of the last round
+        self.strategy, self.params = resolve_strategy()
+
+    # ------------------------------------------------------------------ prefill
+    @torch.inference_mode()
+    def prefill(self, input_ids: torch.Tensor) -> None:
+        """Prompt forward (causal, same kernel) and the first target token."""
+        ids = input_ids.to(self.device)
+        n = ids.shape[1]
+        self.cache.set_length(0)
+        pos = torch.arange(n, device=self.device).unsqueeze(0)
+        out = self.target(ids, position_ids=pos, past_key_values=self.cache, use_cache=True, logits_to_keep=1,
+                          output_hidden_states=self.target_layer_ids is not None)
+        self.output_ids[:n] = ids[0]
+        self.output_ids[n: n + 1] = sample(out.logits, self.temperature)[0]
+        if self.target_layer_ids is not None:
+            self.target_hidden = extract_context_feature(out.hidden_states, self.target_layer_ids)
+        self.start = n
+        self.start_dev.fill_(n)
+
+    # ------------------------------------------------------------------ one round
+    def _tick(self, name, t0):
+        if self.timed:
+            t1 = cuda_time()
+            self.stage_times[name] += t1 - t0
+            return t1
+        return t0
+
+    @torch.inference_mode()
+    def round(self, draft_logits: torch.Tensor, host_walk=None) -> int:
+        """Verify one tree built from ``draft_logits [horizon, vocab]``; returns the accepted length.
+
+        ``host_walk(child_maps, posterior, logits) -> (accepted list, next token)``
+        replaces the device exact walk (ReTree's recovery verifier).
+        """
+        start = self.start
+        if start + self.n_max + 1 > self.output_ids.numel():
+            raise RuntimeError("TreeVerifier max_length exceeded")
+        t = cuda_time() if self.timed else 0.0
+        rows, vocab = draft_logits.shape
+        count = expected_tree_size(self.budget, rows, vocab) if self.budget > 0 else 0
+        n = 1 + count
+        # 1. tree (context = committed ids up to and including the root)
+        if self.budget > 0:
+            build_tree_device(draft_logits, self.budget, self.output_ids, self.strategy, self.params,
+                              out=self.tree, ctx_len=start + 1, start=start)
+        else:
+            self.tree["verify_ids"][0] = self.output_ids[start]
+            self.tree["verify_pos"][0] = start
+            self.tree["mask"][0, 0] = 1
+            self.tree["count"].zero_()
+        t = self._tick("tree_build", t)
+        ids = self.tree["verify_ids"][:n].view(1, n)
+        pos = self.tree["verify_pos"][:n].view(1, n)
+        bits = self.tree["mask"][:n]
+        mask = attach(bits.view(1, 1, n, self.words), bits)
+        t = self._tick("tree_compile", t)
+        # 2. verify forward
+        out = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache, use_cache=True,
+                          output_hidden_states=self.target_layer_ids is not None)
+        t = self._tick("verify", t)
+        # 3.-5. posterior, walk, commit, compaction
+        posterior = sample(out.logits, self.temperature)
+        if self.debug:
+            self.last_posterior = posterior
+            self.last_slab = self.cache.slab[:, :, : start + n, :].clone()
+        if host_walk is None:
+            kernels.tree_walk(self.tree["parents"], self.tree["tokens"], posterior[0], count=count,
+                              out=self.walk, verify_ids=self.tree["verify_ids"], output_ids=self.output_ids,
+                              start_dev=self.start_dev)
+            kernels.kv_compact(self.cache.slab[:, :, : start + n, :], start, self.walk["accepted"], cur_length=n,
+                               n_keep_dev=self.walk["accepted_len"], n_keep=n)
+            acc_len = int(self.walk["accepted_len"].item())
+            accepted = None
+        else:
+            host = torch.cat([self.tree["parents"][:n].to(torch.int64), self.tree["tokens"][:count]]).cpu().tolist()
+            parents, tokens = host[:n], host[n:]
+            maps = [dict() for _ in range(n)]
+            for i in range(1, n):
+                maps[parents[i]][int(tokens[i - 1])] = i
+            accepted, nxt = host_walk(maps, posterior, out.logits)
+            acc_len = len(accepted)
+            keep = torch.tensor(accepted, dtype=torch.long, device=self.device)
+            self.output_ids[start: start + acc_len] = self.tree["verify_ids"].index_select(0, keep)
+            self.output_ids[start + acc_len] = int(nxt)
+            kernels.kv_compact(self.cache.slab[:, :, : start + n, :], start, keep, cur_length=n)
+            self.start_dev.fill_(start + acc_len)
+        self.cache.crop(start)
+        for layer in self.cache.layers:
+            layer.length = start + acc_len
+        if self.target_layer_ids is not None:
+            keep_idx = self.walk["accepted"][:acc_len] if accepted is None else keep
+            self.target_hidden = extract_context_feature(out.hidden_states, self.target_layer_ids).index_select(
+                1, keep_idx)
+        self.start = start + acc_len
+        self._tick("commit", t)
+        return acc_len
+
+    # ------------------------------------------------------------------ decode loop
+    def _draft(self, draft_model, draft_fn, round_idx, block_size):
+        start = self.start
+        if draft_fn is not None:
+            return draft_fn(self.output_ids, start, round_idx)
+        # the reference's draft call (ddtree.py:828-845)
+        block = self.output_ids[start: start + block_size].clone().unsqueeze(0)
+        noise = self.target.model.embed_tokens(block)
+        if not hasattr(self, "_draft_cache"):
+            from transformers import DynamicCache
+            self._draft_cache = DynamicCache()
+            self._positions = torch.arange(self.output_ids.numel(), device=self.device).unsqueeze(0)
+        dc = self._draft_cache
+        hidden = draft_model(target_hidden=self.target_hidden, noise_embedding=noise,
+                             position_ids=self._positions[:, dc.get_seq_length(): start + block_size],
+                             past_key_values=dc, use_cache=True, is_causal=False)[:, -(block_size - 1):, :]
+        logits = self.target.lm_head(hidden)
+        dc.crop(start)
+        return logits[0]
+
+    @torch.inference_mode()
+    def generate(self, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids, draft_model=None,
+                 draft_fn=None, save_tree_traces=False, host_walk=None) -> SimpleNamespace:
+        """The decode loop of ddtree.py:827-968 / retree.py:296-444 on this verifier."""
+        self.timed = True
+        num_input = input_ids.shape[1]
+        max_length = num_input + max_new_tokens
+        self.output_ids.fill_(mask_token_id)
+        stop = None if stop_token_ids is None else torch.tensor(stop_token_ids, device=self.device)
+        t0 = cuda_time()
+        self.prefill(input_ids)
+        ttft = cuda_time() - t0
+        decode_start = cuda_time()
+        acceptance, stamps, traces = [], [], ([] if save_tree_traces else None)
+        r = 0
+        while self.start < max_length:
+            ts = cuda_time()
+            logits = self._draft(draft_model, draft_fn, r, block_size)
+            if r > 0:
+                self.stage_times["draft"] += cuda_time() - ts
+            else:
+                decode_start = cuda_time()
+            acc = self.round(logits, host_walk=host_walk)
+            acceptance.append(acc)
+            stamps.append(cuda_time() - decode_start)
+            if save_tree_traces:
+                cnt = int(self.tree["count"].item())
+                traces.append(dict(
+                    accepted_indices=[] if self.walk is None else self.walk["accepted"][:acc].tolist(),
+                    tree=dict(node_token_ids=self.tree["tokens"][:cnt].tolist(),
+                              node_depths=self.tree["depths"][:cnt].tolist(),
+                              parents=self.tree["parents"][: cnt + 1].tolist())))
+            r += 1
+            if stop is not None:
+                new = self.output_ids[self.start - acc: self.start + 1]
+                if torch.isin(new, stop).any():
+                    break
+        out = self.output_ids[:max_length]
+        out = out[out != mask_token_id].unsqueeze(0)
+        if stop is not None:
+            hits = torch.isin(out[0][num_input:], stop).nonzero(as_tuple=True)[0]
+            if hits.numel() > 0:
+                out = out[:, : num_input + int(hits[0]) + 1]
+        n_out = out.shape[1] - num_input
+        total = cuda_time() - decode_start
+        self.timed = False
+        return SimpleNamespace(output_ids=out.cpu(), num_input_tokens=num_input, num_output_tokens=n_out,
+                               time_to_first_token=ttft, time_per_output_token=total / max(n_out, 1),
+                               acceptance_lengths=acceptance, decode_rounds=len(acceptance),
+                               stage_times=self.stage_times, round_timestamps=stamps, round_trees=traces)
