@@ -66,12 +66,14 @@ const char* rt_status_string(int code);
  * with gather-then-scatter semantics (any order of keep is allowed).  As in
  * the reference, nothing moves when n_keep == 0 or n_keep == cur_len.
  * keep (int64, DEVICE) holds window-relative indices in [0, cur_len).  When
- * n_keep_dev is non-NULL the count is read from it (<= n_keep) at run time.
- * Limit: n_keep * row_bytes <= 200 KiB.
+ * n_keep_dev is non-NULL the count is read from it (<= n_keep) at run time;
+ * when past_len_dev is non-NULL past_len is read from it (int64, DEVICE) and
+ * the host past_len is ignored.  Limit: n_keep * row_bytes <= 200 KiB.
  * ---------------------------------------------------------------------- */
 int rt_kv_compact(void* const* slabs, void* base, int n_slabs, int64_t slab_stride, int n_heads,
-                  int64_t head_stride, int64_t row_stride, int row_bytes, int64_t past_len, int64_t cur_len,
-                  const int64_t* keep, int n_keep, const int32_t* n_keep_dev, int* status, rt_stream_t stream);
+                  int64_t head_stride, int64_t row_stride, int row_bytes, int64_t past_len,
+                  const int64_t* past_len_dev, int64_t cur_len, const int64_t* keep, int n_keep,
+                  const int32_t* n_keep_dev, int* status, rt_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * In-place KV append into a preallocated cache.
@@ -202,8 +204,9 @@ int rt_tree_build(const float* top_logp, const int64_t* top_ids, int rows, int k
  * `keep` of rt_kv_compact), the length to accepted_len (int32) and
  * the target's next token to next_token.  When output_ids is non-NULL it
  * also writes the accepted tokens (verify_ids[accepted[i]]) to
- * output_ids[start + i] and next_token to output_ids[start + len], and
- * advances start_dev[0] by len (start is read from start_dev).
+ * output_ids[start + i] and next_token to output_ids[start + len], advances
+ * start_dev[0] by len and keeps the start before the commit in start_dev[1]
+ * (start_dev then holds two int64; start is read from start_dev[0]).
  * The tree is given by parents (int32[count+1]) and node tokens
  * (int64[count]); count from count_dev when non-NULL, else `count`.
  * ---------------------------------------------------------------------- */

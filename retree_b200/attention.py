@@ -95,12 +95,20 @@ def tree_attention_forward(module, query: torch.Tensor, key: torch.Tensor, value
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)
         ev0.record()
+    # rows allocated per head: the launch (and its split of the keys) is sized
+    # for the cache's capacity, so host-length and device-length rounds over the
+    # same cache run the identical launch
+    cap = key.shape[2]
+    if key.stride(-1) == 1 and key.stride(2) > 0 and key.stride(1) % key.stride(2) == 0:
+        cap = max(cap, key.stride(1) // key.stride(2))
+    splits = kernels.default_splits(n, query.shape[1], key.shape[1], cap - n)
     if prefix_dev is not None:
         # full-capacity K/V views; the real prefix length lives on the device
-        out = kernels.tree_attention(query, key, value, bits, prefix_len=key.shape[2] - n, scale=scaling,
-                                     prefix_len_dev=prefix_dev, kv_capacity=key.shape[2])
+        out = kernels.tree_attention(query, key, value, bits, prefix_len=cap - n, scale=scaling,
+                                     prefix_len_dev=prefix_dev, kv_capacity=cap, num_splits=splits)
     else:
-        out = kernels.tree_attention(query, key, value, bits, prefix_len=key.shape[2] - n, scale=scaling)
+        out = kernels.tree_attention(query, key, value, bits, prefix_len=key.shape[2] - n, scale=scaling,
+                                     kv_capacity=cap, num_splits=splits)
     if PROFILE is not None:
         ev1.record()
         PROFILE.append((ev0, ev1, key.shape[2] - n, n, query.shape[1], key.shape[1]))

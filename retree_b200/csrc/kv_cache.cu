@@ -12,7 +12,8 @@ namespace rt {
 template <typename Unit>
 __global__ void __launch_bounds__(256) kv_compact_kernel(void* const* slabs, char* base, int64_t slab_stride,
                                                          int n_heads, int64_t head_stride, int64_t row_stride,
-                                                         int row_bytes, int64_t past_len, int64_t cur_len,
+                                                         int row_bytes, int64_t past_len_host,
+                                                         const int64_t* past_len_dev, int64_t cur_len,
                                                          const int64_t* __restrict__ keep, int n_keep,
                                                          const int32_t* n_keep_dev, int* status) {
   extern __shared__ __align__(16) unsigned char stage[];
@@ -21,6 +22,7 @@ __global__ void __launch_bounds__(256) kv_compact_kernel(void* const* slabs, cha
   const int head = blockIdx.x % n_heads;
   int nk = n_keep;
   if (n_keep_dev != nullptr) nk = min(max(*n_keep_dev, 0), n_keep);
+  const int64_t past_len = past_len_dev != nullptr ? *past_len_dev : past_len_host;
   // Same no-op rule as the reference: nothing kept, or everything kept.
   if (nk == 0 || nk == cur_len) return;
   if (threadIdx.x == 0) bad = 0;
@@ -30,7 +32,7 @@ __global__ void __launch_bounds__(256) kv_compact_kernel(void* const* slabs, cha
     if (k < 0 || k >= cur_len) bad = 1;
   }
   __syncthreads();
-  if (bad) {
+  if (bad || past_len < 0) {
     if (threadIdx.x == 0) set_status(status, RT_DEV_BAD_INDEX);
     return;
   }
@@ -86,8 +88,8 @@ using namespace rt;
 
 extern "C" int rt_kv_compact(void* const* slabs, void* base, int n_slabs, int64_t slab_stride, int n_heads,
                              int64_t head_stride, int64_t row_stride, int row_bytes, int64_t past_len,
-                             int64_t cur_len, const int64_t* keep, int n_keep, const int32_t* n_keep_dev,
-                             int* status, rt_stream_t stream) {
+                             const int64_t* past_len_dev, int64_t cur_len, const int64_t* keep, int n_keep,
+                             const int32_t* n_keep_dev, int* status, rt_stream_t stream) {
   if (n_slabs < 0 || n_heads < 0 || row_bytes <= 0 || past_len < 0 || cur_len < 0 || n_keep < 0)
     return RT_ERR_INVALID_ARGUMENT;
   if (n_keep > cur_len) return RT_ERR_INVALID_ARGUMENT;  // ddtree.py:55
@@ -106,17 +108,17 @@ extern "C" int rt_kv_compact(void* const* slabs, void* base, int n_slabs, int64_
   if ((align_bits & 15) == 0) {
     set_smem_limit(kv_compact_kernel<uint4>, smem);
     kv_compact_kernel<uint4><<<grid, 256, smem, s>>>(slabs, static_cast<char*>(base), slab_stride, n_heads,
-                                                     head_stride, row_stride, row_bytes, past_len, cur_len, keep,
+                                                     head_stride, row_stride, row_bytes, past_len, past_len_dev, cur_len, keep,
                                                      n_keep, n_keep_dev, status);
   } else if ((align_bits & 3) == 0) {
     set_smem_limit(kv_compact_kernel<uint32_t>, smem);
     kv_compact_kernel<uint32_t><<<grid, 256, smem, s>>>(slabs, static_cast<char*>(base), slab_stride, n_heads,
-                                                        head_stride, row_stride, row_bytes, past_len, cur_len,
+                                                        head_stride, row_stride, row_bytes, past_len, past_len_dev, cur_len,
                                                         keep, n_keep, n_keep_dev, status);
   } else if ((align_bits & 1) == 0) {
     set_smem_limit(kv_compact_kernel<uint16_t>, smem);
     kv_compact_kernel<uint16_t><<<grid, 256, smem, s>>>(slabs, static_cast<char*>(base), slab_stride, n_heads,
-                                                        head_stride, row_stride, row_bytes, past_len, cur_len,
+                                                        head_stride, row_stride, row_bytes, past_len, past_len_dev, cur_len,
                                                         keep, n_keep, n_keep_dev, status);
   } else {
     return RT_ERR_UNSUPPORTED;

@@ -6,7 +6,7 @@ namespace rt {
 thread_local int g_last_cuda_error = 0;
 }
 
-extern "C" int rt_abi_version(void) { return 1; }
+extern "C" int rt_abi_version(void) { return 2; }
 
 extern "C" int rt_last_cuda_error(void) { return rt::g_last_cuda_error; }
 

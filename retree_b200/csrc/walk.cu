@@ -44,7 +44,8 @@ __global__ void tree_walk_kernel(const int32_t* __restrict__ parents, const int6
     for (int i = lane; i < len; i += 32) output_ids[start + i] = verify_ids[accepted[i]];
     if (lane == 0) {
       output_ids[start + len] = nxt;
-      *start_dev = start + len;
+      start_dev[1] = start;
+      start_dev[0] = start + len;
     }
   }
 }

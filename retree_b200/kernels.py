@@ -88,7 +88,8 @@ def check_device_status(device, reset: bool = True) -> None:
 # KV cache
 # ---------------------------------------------------------------------------
 def kv_compact(tensors, past_length: int, keep: torch.Tensor, cur_length: int | None = None,
-               n_keep_dev: torch.Tensor | None = None, n_keep: int | None = None) -> None:
+               n_keep_dev: torch.Tensor | None = None, n_keep: int | None = None,
+               past_len_dev: torch.Tensor | None = None) -> None:
     """In-place compaction of appended rows (ddtree.py:666-731 semantics).
 
     ``tensors``: one ``[..., S, D]`` tensor or a list of them.  All leading
@@ -109,7 +110,7 @@ def kv_compact(tensors, past_length: int, keep: torch.Tensor, cur_length: int | 
         if t.dim() < 2:
             raise RuntimeError("cache_tensor must have rank >= 2")
         seq = t.shape[-2]
-        if past_length < 0 or past_length > seq:
+        if past_len_dev is None and (past_length < 0 or past_length > seq):
             raise RuntimeError("past_length exceeds cache sequence length")
         cur = (seq - past_length) if cur_length is None else int(cur_length)
         if cur <= 0:
@@ -119,12 +120,12 @@ def kv_compact(tensors, past_length: int, keep: torch.Tensor, cur_length: int | 
         try:
             v = t.view(-1, seq, t.shape[-1])
         except RuntimeError:
-            kv_compact(list(t.unbind(0)), past_length, keep, cur_length, n_keep_dev, n_keep)
+            kv_compact(list(t.unbind(0)), past_length, keep, cur_length, n_keep_dev, n_keep, past_len_dev)
             continue
         es = v.element_size()
         rc = lib.rt_kv_compact(None, v.data_ptr(), 1, 0, v.shape[0], v.stride(0) * es, v.stride(1) * es,
-                               v.shape[2] * es, int(past_length), cur, keep.data_ptr(), nk, _ptr(n_keep_dev),
-                               _STATE.status(t.device).data_ptr(), _stream(t.device))
+                               v.shape[2] * es, int(past_length), _ptr(past_len_dev), cur, keep.data_ptr(), nk,
+                               _ptr(n_keep_dev), _STATE.status(t.device).data_ptr(), _stream(t.device))
         _lib.check(rc, "rt_kv_compact")
         _count()
 
@@ -136,8 +137,10 @@ def kv_append(k_cache: torch.Tensor, v_cache: torch.Tensor, k_new: torch.Tensor,
     _require_cuda(k_cache, v_cache, k_new, v_new)
     k_cache, v_cache = _as3(k_cache), _as3(v_cache)
     k_new, v_new = _as3(k_new), _as3(v_new)
-    if k_new.stride() != v_new.stride() or k_cache.stride() != v_cache.stride():
-        raise RuntimeError("K and V must share strides")
+    if k_cache.stride() != v_cache.stride():
+        raise RuntimeError("K and V caches must share strides")
+    if k_new.stride() != v_new.stride():
+        k_new, v_new = k_new.contiguous(), v_new.contiguous()
     es = k_cache.element_size()
     heads, n, d = k_new.shape
     rc = lib.rt_kv_append(k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0) * es, k_cache.stride(1) * es,
@@ -205,6 +208,11 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
     _lib.check(rc, "rt_tree_attn")
     _count(2 if splits > 1 else 1)
     return out
+
+
+def default_splits(n: int, num_q_heads: int, num_kv_heads: int, prefix_len: int) -> int:
+    """Key splits rt_tree_attn picks for this shape (one wave of CTAs)."""
+    return int(_lib.load().rt_tree_attn_default_splits(n, num_q_heads, num_kv_heads, int(prefix_len)))
 
 
 def mask_from_dense(dense: torch.Tensor, col0: int, n: int, words: int | None = None) -> torch.Tensor:

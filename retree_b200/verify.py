@@ -69,7 +69,12 @@ class TreeVerifier:
         self.max_length = int(max_length)
         self.cache = TreeKVCache.for_model(cfg, capacity=self.max_length + self.n_max + 128, device=self.device)
         self.output_ids = torch.zeros(self.max_length + self.n_max + 1, dtype=torch.long, device=self.device)
-        self.start_dev = torch.zeros(1, dtype=torch.int64, device=self.device)
+        # [start, start before the last commit]; in graph mode the cache appends at start_dev[0]
+        self.start_dev = torch.zeros(2, dtype=torch.int64, device=self.device)
+        self.graph_mode = False
+        self.graph = None
+        self.static_logits = None
+        self.launches_per_round = None
         self.start = 0
         self.target_layer_ids = target_layer_ids
         self.target_hidden = None
@@ -98,6 +103,8 @@ class TreeVerifier:
         """Prompt forward (causal, same kernel) and the first target token."""
         ids = input_ids.to(self.device)
         n = ids.shape[1]
+        device_mode = self.cache.device_length
+        self.cache.use_device_length(False)  # the prompt is causal over an empty cache
         self.cache.set_length(0)
         pos = torch.arange(n, device=self.device).unsqueeze(0)
         out = self.target(ids, position_ids=pos, past_key_values=self.cache, use_cache=True, logits_to_keep=1,
@@ -108,6 +115,8 @@ class TreeVerifier:
             self.target_hidden = extract_context_feature(out.hidden_states, self.target_layer_ids)
         self.start = n
         self.start_dev.fill_(n)
+        self.graph = None
+        self.cache.use_device_length(device_mode)
 
     # ------------------------------------------------------------------ one round
     def _tick(self, name, t0):
@@ -117,6 +126,70 @@ class TreeVerifier:
             return t1
         return t0
 
+    # ------------------------------------------------------------------ graph mode
+    def enable_graph(self, enabled: bool = True) -> None:
+        """Run every round as one CUDA-graph replay (after a first eager round that captures it).
+
+        The cache appends at ``start_dev[0]``, the attention reads the prefix
+        length from it, the walk advances it, and compaction reads the
+        pre-commit start from ``start_dev[1]``: no host value of the round
+        changes between rounds, so one capture serves every prefix length.
+        """
+        self.graph_mode = bool(enabled)
+        self.graph = None
+        self.cache.use_device_length(self.graph_mode)
+        if self.graph_mode:
+            self.cache.length_dev = self.start_dev[:1]
+
+    def _round_body(self, logits: torch.Tensor, count: int) -> None:
+        """One round with every varying quantity on the device (capturable)."""
+        n = 1 + count
+        if self.budget > 0:
+            build_tree_device(logits, self.budget, self.output_ids, self.strategy, self.params, out=self.tree,
+                              ctx_len=1, ctx_len_dev=self.start_dev[:1], start_dev=self.start_dev[:1])
+        else:
+            raise RuntimeError("graph mode needs a tree budget > 0")
+        ids = self.tree["verify_ids"][:n].view(1, n)
+        pos = self.tree["verify_pos"][:n].view(1, n)
+        bits = self.tree["mask"][:n]
+        mask = attach(bits.view(1, 1, n, self.words), bits, prefix_dev=self.start_dev[:1])
+        out = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache, use_cache=True)
+        posterior = sample(out.logits, self.temperature)
+        kernels.tree_walk(self.tree["parents"], self.tree["tokens"], posterior[0], count=count, out=self.walk,
+                          verify_ids=self.tree["verify_ids"], output_ids=self.output_ids, start_dev=self.start_dev)
+        kernels.kv_compact(self.cache.slab, 0, self.walk["accepted"], cur_length=n,
+                           n_keep_dev=self.walk["accepted_len"], n_keep=n, past_len_dev=self.start_dev[1:2])
+
+    def _graph_round(self, draft_logits: torch.Tensor) -> int:
+        rows, vocab = draft_logits.shape
+        count = expected_tree_size(self.budget, rows, vocab)
+        if self.start + self.n_max + 1 > self.output_ids.numel():
+            raise RuntimeError("TreeVerifier max_length exceeded")
+        if self.graph is None:
+            self.static_logits = torch.empty_like(draft_logits).contiguous()
+            self.static_logits.copy_(draft_logits)
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                self._round_body(self.static_logits, count)  # real round, and warm-up for the capture
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            acc = int(self.walk["accepted_len"].item())
+            before = kernels.LAUNCHES
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=side):
+                self._round_body(self.static_logits, count)
+            self.launches_per_round = kernels.LAUNCHES - before
+            self.graph = g
+        else:
+            self.static_logits.copy_(draft_logits, non_blocking=True)
+            self.graph.replay()
+            kernels._count(self.launches_per_round)
+            acc = int(self.walk["accepted_len"].item())
+        self.start += acc
+        for layer in self.cache.layers:
+            layer.length = self.start
+        return acc
+
     @torch.inference_mode()
     def round(self, draft_logits: torch.Tensor, host_walk=None) -> int:
         """Verify one tree built from ``draft_logits [horizon, vocab]``; returns the accepted length.
@@ -124,6 +197,10 @@ class TreeVerifier:
         ``host_walk(child_maps, posterior, logits) -> (accepted list, next token)``
         replaces the device exact walk (ReTree's recovery verifier).
         """
+        if self.graph_mode and host_walk is None and not self.timed:
+            return self._graph_round(draft_logits)
+        if self.graph_mode:
+            raise RuntimeError("graph mode runs the exact device walk without stage timers")
         start = self.start
         if start + self.n_max + 1 > self.output_ids.numel():
             raise RuntimeError("TreeVerifier max_length exceeded")

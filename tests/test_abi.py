@@ -28,7 +28,7 @@ def test_library_loads_and_exports_every_declared_symbol():
     for name in decls:
         assert hasattr(lib, name), name
     assert set(decls) == set(_lib.SIGNATURES)
-    assert lib.rt_abi_version() == 1
+    assert lib.rt_abi_version() == 2
 
 
 def test_ctypes_signatures_match_header():
@@ -62,7 +62,7 @@ def test_status_strings():
 def test_host_argument_checks_need_no_gpu():
     lib = _lib.load()
     # negative sizes and keep > window are rejected before any launch
-    assert lib.rt_kv_compact(None, None, 1, 0, 1, 0, 0, 256, 0, 4, None, 5, None, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_kv_compact(None, None, 1, 0, 1, 0, 0, 256, 0, None, 4, None, 5, None, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
     assert lib.rt_tree_attn(None, 0, 0, None, None, 0, 0, 0, None, 0, 0, None, 1, 1, 0, None, 32, 8, 128, 1.0,
                             0, 0, None, 0, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
     assert lib.rt_draft_topk(None, 0, 10, 1, 10, 2000, None, None, None, None, 0, None) == _lib.RT_ERR_UNSUPPORTED

@@ -174,3 +174,27 @@ def test_tree_decoding_equals_greedy_decoding(monkeypatch):
     got = res.output_ids[0, 64:].tolist()
     assert got[: len(greedy)] == greedy[: len(got)]
     assert res.num_output_tokens >= new
+
+
+@torch.inference_mode()
+def test_graph_rounds_equal_eager_rounds(models, monkeypatch):
+    """A CUDA-graph replay of the round is bit-identical to the eager round."""
+    monkeypatch.setenv("DDTREE_TREE_STRATEGY", "rank_gated_ngram")
+    ours, _ = models
+    dev = cuda()
+    prompt = torch.from_numpy(synthetic.context_ids(8, 150, VOCAB, alphabet=40))[None].to(dev)
+    drafts = [torch.from_numpy(synthetic.draft_logits(300 + r, 15, VOCAB, amp=6.0)).to(dev).to(torch.bfloat16)
+              for r in range(6)]
+    eager = TreeVerifier(ours, tree_budget=24, max_length=500, draft_horizon=15)
+    eager.prefill(prompt)
+    graph = TreeVerifier(ours, tree_budget=24, max_length=500, draft_horizon=15)
+    graph.prefill(prompt)
+    graph.enable_graph(True)
+    for d in drafts:
+        a = eager.round(d)
+        b = graph.round(d)
+        assert a == b and eager.start == graph.start
+    s = eager.start
+    assert torch.equal(eager.output_ids[: s + 1], graph.output_ids[: s + 1])
+    assert torch.equal(eager.cache.slab[:, :, :s], graph.cache.slab[:, :, :s])
+    assert graph.launches_per_round and graph.graph is not None
