@@ -132,6 +132,31 @@ int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, con
 int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len);
 
 /* ------------------------------------------------------------------------
+ * Tree-verify attention that allocates nothing.
+ * No counterpart in the reference: an addition for callers that cannot
+ * allocate device memory at the call -- code running during CUDA stream
+ * capture (cudaMalloc is not allowed there), serving runtimes whose device
+ * memory is all pre-reserved by their own pool, and C hosts with no allocator
+ * to supply rt_tree_attn's workspace.
+ *
+ * Same arguments and results as rt_tree_attn without the workspace: the split
+ * partials go to a fixed 16 MiB device array inside this library
+ * (rt_tree_attn_noalloc_max_bytes()), held by every GPU that loads the
+ * library until the process exits.  A shape whose rt_tree_attn_workspace_size
+ * exceeds it returns RT_ERR_WORKSPACE.  The first call on a device looks the
+ * array's address up for that device (that device must be current), so it
+ * must come before any stream capture.  Every call shares the one array:
+ * calls that overlap on the GPU race on it.
+ * ---------------------------------------------------------------------- */
+size_t rt_tree_attn_noalloc_max_bytes(void);
+int rt_tree_attn_noalloc(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
+                         int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
+                         int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words,
+                         int n, int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads,
+                         int num_kv_heads, int head_dim, float scale, int num_splits, int path, int* status,
+                         rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Packed ancestor bitmask from a dense additive mask.
  * Replaces reading the tree block of the mask compile_ddtree_tree writes
  * (ddtree.py:629-640): bit j of row i is set iff

@@ -31,6 +31,9 @@ SIGNATURES = {
     "rt_tree_attn": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                           _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P]),
     "rt_tree_attn_default_splits": (_I, [_I, _I, _I, _I64]),
+    "rt_tree_attn_noalloc_max_bytes": (_SZ, []),
+    "rt_tree_attn_noalloc": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
+                                  _I, _I, _I, _F, _I, _I, _P, _P]),
     "rt_mask_from_dense": (_I, [_P, _I, _I64, _I64, _I, _P, _I, _P]),
     "rt_draft_topk_workspace_size": (_SZ, [_I, _I, _I]),
     "rt_draft_topk": (_I, [_P, _I, _I64, _I, _I, _I, _P, _P, _P, _P, _SZ, _P]),

@@ -27,6 +27,8 @@
 #include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "host_util.h"
 
@@ -816,4 +818,74 @@ extern "C" int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_
   const int warps = num_kv_heads * n * G;
   attn_combine_kernel<<<(warps + 3) / 4, 128, 0, s>>>(p);
   return check_launch();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant: the split partials live in a fixed device array.
+//
+// Some callers cannot allocate device memory when they call this kernel:
+// code that runs while a CUDA stream is being captured into a graph (a
+// cudaMalloc there is not allowed), serving runtimes that hand every byte of
+// device memory to their own pool up front, and plain C hosts that bind only
+// this ABI and have no allocator to carve a workspace from.  For them the
+// scratch is a file-scope __device__ array of kNoAllocScratchBytes that every
+// GPU loading this library holds until the process exits.
+//
+// Its device address is looked up once per device (cudaGetSymbolAddress with
+// that device current) on the first call on that device, so that first call
+// must not be made while a stream is being captured.  All calls share the one
+// array: calls whose launches overlap on the GPU (different streams, or
+// different host threads) race on it.  Nothing in it has to start at zero --
+// every split writes all of its partial rows (or its neutral -inf/0 row)
+// before the merge reads them -- and it keeps the last call's contents.
+// ---------------------------------------------------------------------------
+namespace rt {
+constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;  // 16 MiB
+static __device__ __align__(256) unsigned char g_attn_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+static void* g_scratch_ptr[kMaxDevices] = {};
+static std::mutex g_scratch_mutex;
+
+static int scratch_for_current_device(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return record_cuda(e);
+  if (dev < 0 || dev >= kMaxDevices) return RT_ERR_UNSUPPORTED;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_scratch);  // host code must not use the symbol itself
+    if (e != cudaSuccess) return record_cuda(e);
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return RT_OK;
+}
+}  // namespace rt
+
+extern "C" size_t rt_tree_attn_noalloc_max_bytes(void) { return rt::kNoAllocScratchBytes; }
+
+extern "C" int rt_tree_attn_noalloc(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k,
+                                    const void* v, int64_t kv_head_stride, int64_t kv_row_stride,
+                                    int64_t kv_capacity, void* out, int64_t out_tok_stride, int64_t out_head_stride,
+                                    const uint32_t* mask, int mask_words, int n, int64_t prefix_len,
+                                    const int64_t* prefix_len_dev, int num_q_heads, int num_kv_heads, int head_dim,
+                                    float scale, int num_splits, int path, int* status, rt_stream_t stream) {
+  if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || head_dim <= 0)
+    return RT_ERR_INVALID_ARGUMENT;
+  if (num_splits <= 0) {
+    const int G = num_q_heads / num_kv_heads;
+    num_splits = rt::default_splits(n, G, num_kv_heads, prefix_len, rt::use_tc(n, G, path));
+  }
+  const size_t need = rt_tree_attn_workspace_size(n, num_q_heads, num_kv_heads, head_dim, prefix_len, num_splits);
+  if (need > rt::kNoAllocScratchBytes) return RT_ERR_WORKSPACE;  // beyond the fixed scratch: use rt_tree_attn
+  void* ws = nullptr;
+  if (need > 0) {
+    const int rc = rt::scratch_for_current_device(&ws);
+    if (rc != RT_OK) return rc;
+  }
+  return rt_tree_attn(q, q_tok_stride, q_head_stride, k, v, kv_head_stride, kv_row_stride, kv_capacity, out,
+                      out_tok_stride, out_head_stride, mask, mask_words, n, prefix_len, prefix_len_dev, num_q_heads,
+                      num_kv_heads, head_dim, scale, num_splits, path, ws, need, status, stream);
 }
