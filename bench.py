@@ -240,11 +240,13 @@ def run_ours(args, wl, rank, world, local_rank):
     accepted = []
 
     def rounds_resident():
+        torch.cuda.nvtx.range_push("timed_rounds")
         ev0.record()
         for i in range(steps):
             accepted.append(v.round(resident[warm + i]))
             exchange()
         ev1.record()
+        torch.cuda.nvtx.range_pop()
 
     wall = timed(rounds_resident)
     clocks = sampler.stop() if sampler else None

@@ -1,0 +1,160 @@
+"""Kernel-level measurements of the verification path (one JSON line per case).
+
+    python -m retree_b200.bench_kernels sweep  [--prefix 4096] [--budgets 16,32,64,128,256] [--layers 36]
+    python -m retree_b200.bench_kernels single --budget 16 --prefix 2048 [--reps 3]
+    python -m retree_b200.bench_kernels parts
+
+``sweep`` is the tree-verify attention budget sweep (Qwen3-4B head geometry:
+32 query / 8 KV heads, head_dim 128, bf16): random trees from seeded parent
+arrays (depth <= 16, Geometric(0.5) branching), K/V ~ N(0,1), one KV cache per
+layer so consecutive launches stream from HBM (36 x (L+n) x 4 KiB > L2), all
+layers captured in one CUDA graph and timed with CUDA events.  Each line
+reports the algorithmic bytes and FLOPs per launch, the achieved GB/s and
+TFLOP/s, and both as fractions of the measured peaks (MEASURED_PEAKS.json).
+``single`` runs a few launches of one shape (for ncu captures); ``parts``
+times the draft top-k, the tree build and the compaction kernels.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import numpy as np
+import torch
+
+from . import kernels, synthetic
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HQ, HKV, HD = 32, 8, 128
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def attn_bytes(L, n):
+    return (L + n) * 2 * HKV * HD * 2 + 2 * n * HQ * HD * 2 + n * ((n + 31) // 32) * 4
+
+
+def attn_flops(L, n):
+    return 4 * HQ * HD * n * (L + n)
+
+
+def tree_bits(seed: int, n: int, device) -> torch.Tensor:
+    parents = synthetic.random_tree_parents(seed, n - 1, max_depth=16, p=0.5)
+    n = len(parents)
+    vis = np.zeros((n, n), dtype=np.bool_)
+    vis[0, 0] = True
+    for i in range(1, n):
+        vis[i, :i] = vis[parents[i], :i]
+        vis[i, i] = True
+    w = (n + 31) // 32
+    padded = np.zeros((n, w * 32), dtype=np.bool_)
+    padded[:, :n] = vis
+    return torch.from_numpy(np.packbits(padded, axis=1, bitorder="little").view("<u4").view(np.int32)).to(device)
+
+
+def graph_time_us(fn, reps: int = 20) -> float:
+    fn()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        fn()
+    for _ in range(3):
+        g.replay()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    return 1000.0 * e0.elapsed_time(e1) / reps
+
+
+def attention_case(n: int, L: int, layers: int, dev, seed: int = 0, splits: int = 0) -> dict:
+    bits = tree_bits(seed + n, n, dev)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    caches = [torch.randn((2, HKV, L + n, HD), device=dev, generator=g).to(torch.bfloat16) for _ in range(layers)]
+    q = torch.randn((1, HQ, n, HD), device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty((n, HQ, HD), device=dev, dtype=torch.bfloat16)
+    sp = splits or kernels.default_splits(n, HQ, HKV, L)
+
+    def run():
+        for c in caches:
+            kernels.tree_attention(q, c[0], c[1], bits, L, out=out, num_splits=sp)
+
+    us = graph_time_us(run) / layers
+    kernels.check_device_status(dev)
+    hbm, tf, kind = peaks()
+    b, f = attn_bytes(L, n), attn_flops(L, n)
+    gbs, tfs = b / us / 1e3, f / us / 1e6
+    return dict(kernel="tree_attn", budget=n - 1, nodes=n, prefix=L, layers=layers, splits=sp, us_per_launch=us,
+                bytes_per_launch=b, flops_per_launch=f, gbs=gbs, tflops=tfs, hbm_frac=gbs / hbm,
+                tensor_frac=tfs / tf, bound="hbm" if b / hbm > f / (tf * 1e3) else "tensor", peak_kind=kind,
+                path="tcgen05" if n * (HQ // HKV) >= 64 else "warp")
+
+
+def parts(dev) -> list[dict]:
+    from .ddtree import NgramParams
+    out = []
+    logits = torch.from_numpy(synthetic.draft_logits(0, 16, 151936)[-15:]).to(dev).to(torch.bfloat16)
+    ctx = torch.from_numpy(synthetic.context_ids(0, 2049, 151936)).to(dev)
+    for budget in (16, 64, 256):
+        us = graph_time_us(lambda: kernels.draft_topk(logits, budget))
+        out.append(dict(kernel="draft_topk", budget=budget, rows=15, vocab=151936, us=us,
+                        gbs=15 * 151936 * 2 / us / 1e3))
+        lp, ids, _ = kernels.draft_topk(logits, budget)
+        buf = {}
+        tree = kernels.tree_build(lp, ids, budget, "rank_gated_ngram", NgramParams.from_env({}), ctx=ctx, out=None)
+        buf.update(tree)
+        us = graph_time_us(lambda: kernels.tree_build(lp, ids, budget, "rank_gated_ngram",
+                                                      NgramParams.from_env({}), ctx=ctx, out=buf))
+        out.append(dict(kernel="tree_build", strategy="rank_gated_ngram", budget=budget, context=2049, us=us))
+    slab = torch.randn((72, 8, 4096 + 17, 128), device=dev).to(torch.bfloat16)
+    keep = torch.tensor([0, 1, 3, 7, 9, 12, 15], dtype=torch.long, device=dev)
+    us = graph_time_us(lambda: kernels.kv_compact(slab, 4096, keep))
+    moved = 72 * 8 * len(keep) * 256 * 2
+    out.append(dict(kernel="kv_compact", layers=36, kept=len(keep), us=us, bytes_moved=moved, gbs=moved / us / 1e3))
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("mode", choices=("sweep", "single", "parts"))
+    ap.add_argument("--prefix", type=int, default=4096)
+    ap.add_argument("--budgets", default="16,32,64,128,256")
+    ap.add_argument("--budget", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--reps", type=int, default=3)
+    ap.add_argument("--splits", type=int, default=0)
+    a = ap.parse_args()
+    dev = torch.device("cuda:0")
+    torch.cuda.set_device(dev)
+    if a.mode == "sweep":
+        for b in (int(x) for x in a.budgets.split(",")):
+            print(json.dumps(attention_case(b + 1, a.prefix, a.layers, dev, splits=a.splits)), flush=True)
+    elif a.mode == "single":
+        n = a.budget + 1
+        bits = tree_bits(n, n, dev)
+        c = torch.randn((2, HKV, a.prefix + n, HD), device=dev).to(torch.bfloat16)
+        q = torch.randn((1, HQ, n, HD), device=dev).to(torch.bfloat16)
+        for _ in range(a.reps):
+            kernels.tree_attention(q, c[0], c[1], bits, a.prefix, num_splits=a.splits)
+        torch.cuda.synchronize()
+        kernels.check_device_status(dev)
+        print(json.dumps(dict(ok=True, budget=a.budget, prefix=a.prefix)))
+    else:
+        for row in parts(dev):
+            print(json.dumps(row), flush=True)
+
+
+if __name__ == "__main__":
+    main()
