@@ -47,6 +47,8 @@ WORKLOADS = {
     "qwen3-4b-b16": dict(model="qwen3-4b", prompt=2048, budget=16, block=16),
     "qwen3-4b-b64": dict(model="qwen3-4b", prompt=2048, budget=64, block=16),
     "qwen3-8b-b64": dict(model="qwen3-8b", prompt=4096, budget=64, block=16),
+    # one long request split by KV head over the ranks (random N(0,1) KV prefix, no prompt forward)
+    "qwen3-8b-l32k-b256-split": dict(model="qwen3-8b", prompt=32768, budget=256, block=16, split=True),
 }
 DELTA_PAIRS = 4096  # recovery-memory delta exchanged per step at N>1 (int32 draft, target, count)
 
@@ -190,27 +192,38 @@ def run_ours(args, wl, rank, world, local_rank):
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     cfg = qwen3_config(wl["model"])
-    target = build_target(cfg, device=dev, seed=0)
+    split = bool(wl.get("split")) and world > 1
+    if split:
+        from retree_b200 import headsplit
+        headsplit.register()
+        target = build_target(cfg, device=dev, seed=0, attn_implementation=headsplit.NAME)
+        headsplit.shard_attention_heads(target, rank, world)
+    else:
+        target = build_target(cfg, device=dev, seed=0)
     steps, warm = args.steps, args.warmup
     total_rounds = warm + steps
     max_len = wl["prompt"] + total_rounds * (wl["block"] + 2) + 64
     # draft logits for every round: bf16 as the lm_head emits them; pinned host copies for the e2e leg
-    host = [torch.from_numpy(draft_logits_np(1000 + 7919 * rank + i, wl["block"], cfg.vocab_size)).to(torch.bfloat16)
+    req = 0 if wl.get("split") else rank  # a split request is the same request on every rank
+    host = [torch.from_numpy(draft_logits_np(1000 + 7919 * req + i, wl["block"], cfg.vocab_size)).to(torch.bfloat16)
             for i in range(total_rounds)]
     pinned = [h.pin_memory() for h in host]
     resident = [h.to(dev) for h in host]
-    prompt = torch.from_numpy(np.random.default_rng(rank).integers(0, cfg.vocab_size, size=wl["prompt"]))[None]
+    prompt = torch.from_numpy(np.random.default_rng(req).integers(0, cfg.vocab_size, size=wl["prompt"]))[None]
 
     def fresh():
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1)
-        v.prefill(prompt.to(dev))
+        if wl.get("split"):
+            v.prefill_random(wl["prompt"], seed=req)
+        else:
+            v.prefill(prompt.to(dev))
         return v
 
     delta_send = torch.zeros((DELTA_PAIRS, 3), dtype=torch.int32, device=dev)
     delta_recv = torch.zeros((world, DELTA_PAIRS, 3), dtype=torch.int32, device=dev) if world > 1 else None
 
     def exchange():
-        if world > 1:
+        if world > 1 and not wl.get("split"):
             dist.all_gather_into_tensor(delta_recv.view(world * DELTA_PAIRS, 3), delta_send)
 
     def barrier():
@@ -262,6 +275,8 @@ def run_ours(args, wl, rank, world, local_rank):
     L_live = v.start
     cap = v.cache.capacity
     hq, hkv = cfg.num_attention_heads, cfg.num_key_value_heads
+    if split:  # each rank attends over its own heads only
+        hq, hkv = hq // world, hkv // world
     q_probe = torch.randn((1, hq, n_tree, 128), device=dev, dtype=torch.bfloat16)
     bits = v.tree["mask"][:n_tree].clone()
     plen = torch.tensor([L_live], dtype=torch.int64, device=dev)
@@ -334,16 +349,19 @@ def run_ours(args, wl, rank, world, local_rank):
                "sample": (f"{args.cpu_sample_rounds} verify rounds ({secs:.1f} s) of the reference path on the host "
                           f"CPU: oracle tree build, dense-mask compile, HF sdpa forward (bf16), walk, compaction, "
                           f"random-KV prefix of {wl['prompt']} tokens")}
-    value = world * steps / dev_s
+    reqs = 1 if wl.get("split") else world  # a split request is one request over all ranks
+    value = reqs * steps / dev_s
     print(json.dumps({
         "metric": "verify rounds/sec", "value": value, "unit": "rounds/s", "n_gpus": world, "steps": steps,
-        "warmup": warm, "ms_per_step": 1000.0 * dev_s / steps, "higher_is_better": True, "scaling": "weak",
+        "warmup": warm, "ms_per_step": 1000.0 * dev_s / steps, "higher_is_better": True,
+        "scaling": "strong" if wl.get("split") else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded draft logits, uniform prompt, random-init "
                                                       "weights)",
         "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": wl["prompt"],
                    "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
-                   "parallelism": f"dp{world} (one request per GPU)" + (
-                       ", recovery-delta all-gather per step" if world > 1 else ""),
+                   "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer)"
+                                   if wl.get("split") else f"dp{world} (one request per GPU)" + (
+                                       ", recovery-delta all-gather per step" if world > 1 else "")),
                    "l2": "inputs > L2 (8 GB of weights and the KV cache stream every round)",
                    "mean_accepted": sum(accepted) / len(accepted), "wall_s": wall},
         "roofline": {"kernel": "tree_attn (rt_tree_attn + split combine)", "bound": "hbm", "achieved": achieved,
@@ -352,7 +370,7 @@ def run_ours(args, wl, rank, world, local_rank):
                      "prefix_len": L_live, "tree_nodes": n_tree, "key_splits": splits,
                      "share_of_round": cfg.num_hidden_layers * attn_us * 1e-3 / (1000.0 * dev_s / steps)},
         "cpu_baseline": cpu,
-        "e2e": {"value": world * steps / e2e_s, "unit": "rounds/s", "h2d_bytes_per_step": h2d,
+        "e2e": {"value": reqs * steps / e2e_s, "unit": "rounds/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "clocks": clocks,

@@ -30,6 +30,7 @@ import torch
 
 from . import kernels
 from .attention import NAME as ATTN_NAME
+from .headsplit import NAME as HEADSPLIT_NAME
 from .attention import attach
 from .cache import TreeKVCache
 from .ddtree import (DDTREE_STAGE_ORDER, DDTREE_TREE_BUILD_STAGE_ORDER, build_tree_device, cuda_time,
@@ -57,7 +58,7 @@ class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
                  temperature: float = 0.0, target_layer_ids=None, device=None):
         cfg = target.config
-        if getattr(cfg, "_attn_implementation", None) != ATTN_NAME:
+        if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
         self.target = target
         self.device = torch.device(device) if device is not None else next(target.parameters()).device
@@ -67,7 +68,11 @@ class TreeVerifier:
         self.n_max = 1 + self.budget
         self.words = (self.n_max + 31) // 32
         self.max_length = int(max_length)
-        self.cache = TreeKVCache.for_model(cfg, capacity=self.max_length + self.n_max + 128, device=self.device)
+        # a target split by KV head (retree_b200.headsplit) caches only its own heads
+        kv_heads = getattr(target, "_rt_local_kv_heads", cfg.num_key_value_heads)
+        head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        self.cache = TreeKVCache(cfg.num_hidden_layers, kv_heads, head_dim, self.max_length + self.n_max + 128,
+                                 device=self.device)
         self.output_ids = torch.zeros(self.max_length + self.n_max + 1, dtype=torch.long, device=self.device)
         # [start, start before the last commit]; in graph mode the cache appends at start_dev[0]
         self.start_dev = torch.zeros(2, dtype=torch.int64, device=self.device)
@@ -117,6 +122,24 @@ class TreeVerifier:
         self.start_dev.fill_(n)
         self.graph = None
         self.cache.use_device_length(device_mode)
+
+    @torch.inference_mode()
+    def prefill_random(self, length: int, seed: int = 0, vocab: int | None = None) -> None:
+        """A synthetic committed prefix: N(0,1) K/V rows and uniform ids (no prompt forward).
+
+        For long-context measurements (a 32K-token prompt forward would dominate
+        and the round's work does not depend on the cached values).
+        """
+        vocab = vocab or self.target.config.vocab_size
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        slab = self.cache.slab
+        for i in range(slab.shape[0]):
+            slab[i, :, :length].copy_(torch.randn(slab[i, :, :length].shape, device=self.device, generator=g))
+        self.output_ids[: length + 1] = torch.randint(0, vocab, (length + 1,), device=self.device, generator=g)
+        self.cache.set_length(length)
+        self.start = length
+        self.start_dev.fill_(length)
+        self.graph = None
 
     # ------------------------------------------------------------------ one round
     def _tick(self, name, t0):
