@@ -335,6 +335,10 @@ def run_ours(args, wl, rank, world, local_rank):
     h2d = host[0].numel() * host[0].element_size()
     d2h = 8 * (wl["budget"] + 2) + 4  # committed tokens + accepted count
 
+    # graphs that captured NCCL calls are released before the process group goes away
+    v.graph = None
+    v2.graph = None
+    torch.cuda.synchronize()
     if rank != 0:
         return
     hbm_peak, tf_peak, peak_kind = measured_peaks()
