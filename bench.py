@@ -181,6 +181,11 @@ def attn_bytes(L: int, n: int, hq: int, hkv: int, hd: int = 128) -> int:
     return (L + n) * 2 * hkv * hd * 2 + 2 * n * hq * hd * 2 + n * ((n + 31) // 32) * 4
 
 
+def log(rank: int, msg: str) -> None:
+    """Per-rank progress on stderr (the JSON line stays alone on stdout)."""
+    print(f"[bench r{rank} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def run_ours(args, wl, rank, world, local_rank):
     import torch.distributed as dist
 
@@ -199,7 +204,8 @@ def run_ours(args, wl, rank, world, local_rank):
         target = build_target(cfg, device=dev, seed=0, attn_implementation=headsplit.NAME)
         headsplit.shard_attention_heads(target, rank, world)
     else:
-        target = build_target(cfg, device=dev, seed=0)
+        log(rank, "target built")
+    target = build_target(cfg, device=dev, seed=0)
     steps, warm = args.steps, args.warmup
     total_rounds = warm + steps
     max_len = wl["prompt"] + total_rounds * (wl["block"] + 2) + 64
@@ -241,12 +247,14 @@ def run_ours(args, wl, rank, world, local_rank):
             dist.all_reduce(dt, op=dist.ReduceOp.MAX)
         return float(dt.item())
 
+    log(rank, "inputs ready")
     # ---- device-resident rounds (value): every round is one CUDA-graph replay ----
     v = fresh()
     v.enable_graph(not args.eager)
     for i in range(warm):
         v.round(resident[i])
         exchange()
+    log(rank, "warm-up rounds done")
     kernels.LAUNCHES = 0
     sampler = ClockSampler(dev.index) if rank == 0 else None
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -270,6 +278,7 @@ def run_ours(args, wl, rank, world, local_rank):
         dist.all_reduce(dev_ms, op=dist.ReduceOp.MAX)
     dev_s = float(dev_ms.item()) / 1000.0
 
+    log(rank, "timed rounds done")
     # ---- the tree-attention kernel on the live cache: all layers back to back, as in the round ----
     n_tree = 1 + wl["budget"]
     L_live = v.start
@@ -292,7 +301,7 @@ def run_ours(args, wl, rank, world, local_rank):
     side = torch.cuda.Stream(dev)
     side.wait_stream(torch.cuda.current_stream(dev))
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=side):
+    with torch.cuda.graph(g, stream=side, capture_error_mode="thread_local"):
         attn_all_layers()
     for _ in range(3):
         g.replay()
@@ -307,6 +316,7 @@ def run_ours(args, wl, rank, world, local_rank):
     byts = attn_bytes(L_live, n_tree, hq, hkv)
     del g
 
+    log(rank, "attention probe done")
     # ---- end to end through the public API: host draft logits in, committed tokens out ----
     v2 = fresh()
     v2.enable_graph(not args.eager)
@@ -328,6 +338,7 @@ def run_ours(args, wl, rank, world, local_rank):
         e1.record()
 
     timed(rounds_e2e)
+    log(rank, "e2e rounds done")
     e2e_ms = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
@@ -392,8 +403,12 @@ def main():
         return
     if world > 1:
         import torch.distributed as dist
+        # the per-step exchanges are tiny all-gathers: no NVLink multicast objects needed
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         torch.cuda.set_device(local_rank)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+        log(rank, "process group up")
     try:
         run_ours(args, wl, rank, world, local_rank)
     finally:

@@ -66,7 +66,7 @@ def graph_time_us(fn, reps: int = 20) -> float:
     side = torch.cuda.Stream()
     side.wait_stream(torch.cuda.current_stream())
     g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=side):
+    with torch.cuda.graph(g, stream=side, capture_error_mode="thread_local"):
         fn()
     for _ in range(3):
         g.replay()

@@ -199,7 +199,7 @@ class TreeVerifier:
             acc = int(self.walk["accepted_len"].item())
             before = kernels.LAUNCHES
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=side):
+            with torch.cuda.graph(g, stream=side, capture_error_mode="thread_local"):
                 self._round_body(self.static_logits, count)
             self.launches_per_round = kernels.LAUNCHES - before
             self.graph = g
