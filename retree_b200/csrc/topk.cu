@@ -232,40 +232,38 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(int vocab, int
   int* idx = reinterpret_cast<int*>(keys + total);
   unsigned long long* srt = reinterpret_cast<unsigned long long*>(
       smem_raw + ((static_cast<size_t>(total) * 8 + 15) & ~static_cast<size_t>(15)));
-  {
-    int off = 0;
-    for (int c = 0; c < n_chunks; ++c) {
-      const int kc = min(k, min(chunk_len, vocab - c * chunk_len));
-      const int64_t base = (static_cast<int64_t>(row) * n_chunks + c) * k;
-      for (int i = tid; i < kc; i += kTopkThreads) {
-        keys[off + i] = cand_key[base + i];
-        idx[off + i] = cand_idx[base + i];
-      }
-      off += kc;
-    }
+  // every chunk but the last contributed exactly k survivors, in chunk order
+  for (int j = tid; j < total; j += kTopkThreads) {
+    const int c = j / k, i = j - c * k;
+    const int64_t base = (static_cast<int64_t>(row) * n_chunks + c) * k;
+    keys[j] = cand_key[base + i];
+    idx[j] = cand_idx[base + i];
   }
-  if (tid == 0) {
+  if (tid < 32) {
+    // logsumexp of the chunk partials (binary64), one warp
     double M = -INFINITY;
     bool nan = false;
-    for (int c = 0; c < n_chunks; ++c) {
+    for (int c = tid; c < n_chunks; c += 32) {
       const double mc = lse_part[row * n_chunks + c].x;
       if (mc != mc) nan = true;
       else M = fmax(M, mc);
     }
-    double lz;
-    if (nan) {
-      lz = NAN;
-    } else if (M == INFINITY || M == -INFINITY) {
-      lz = M;
-    } else {
-      double S = 0.0;
-      for (int c = 0; c < n_chunks; ++c) {
-        const double2 p = lse_part[row * n_chunks + c];
-        if (p.x > -INFINITY) S += p.y * exp(p.x - M);
+    nan = __any_sync(0xFFFFFFFFu, nan);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmax(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
+    double S = 0.0;
+    if (!nan && M > -INFINITY && M < INFINITY) {
+      for (int c = tid; c < n_chunks; c += 32) {
+        const double2 pc = lse_part[row * n_chunks + c];
+        if (pc.x > -INFINITY) S += pc.y * exp(pc.x - M);
       }
-      lz = M + log(S);
     }
-    log_z_sh = static_cast<float>(lz);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xFFFFFFFFu, S, o);
+    if (tid == 0) {
+      const double lz = nan ? static_cast<double>(NAN) : ((M == INFINITY || M == -INFINITY) ? M : M + log(S));
+      log_z_sh = static_cast<float>(lz);
+    }
   }
   __syncthreads();
   // select the row's top k (in index order), staging them in the sort buffer

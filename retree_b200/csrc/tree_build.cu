@@ -1,24 +1,32 @@
 // Budgeted best-first tree expansion on the device (one CTA per request).
 //
-// Prologue (whole CTA): copy the context window to shared memory and sort the
-// (token, position) pairs of every "next" position, so the n-gram count of
-// any (tail, token) is a search for the token's run plus a scan of its
-// occurrences.  Expansion (warp 0): the frontier lives in shared memory as a
-// struct of arrays; each pop is a warp-wide arg-max over it, followed by the
-// reference's sibling/child pushes.  Scores use binary64 with the reference's
-// operation order (fp32 log-probs widened exactly, no fused multiply-adds), and
-// the arg-max breaks ties exactly as the reference's heap tuples do, so the
-// emitted tree is bit-identical.
+// Prologue (whole CTA): the context window goes to shared memory and every
+// n-gram of it (orders 2..max_n) is counted into a shared-memory open-addressing
+// hash table, so the count of any (tail, token) is one short probe sequence per
+// order.  The draft top-k (log-probs and ids) is staged in shared memory when
+// it fits.
+//
+// Expansion (warp 0): the frontier is a compact struct of arrays in shared
+// memory (a popped entry is replaced by the last one).  Each pop is a warp
+// arg-max over it, then the reference's sibling / child pushes; the continuity
+// bonuses of the two pushes are looked up at the same time on different lanes
+// (one lane per n-gram order).  Scores use binary64 in the reference's
+// operation order (fp32 log-probs widened exactly, explicit round-to-nearest
+// adds/multiplies, no contraction) and the arg-max breaks ties as the
+// reference's heap tuples do, so the tree is bit-identical.
 #include "common.cuh"
 #include "host_util.h"
 
 namespace rt {
 
 constexpr int kBuildThreads = 256;
-constexpr int kMaxTail = 7;       // max_n - 1 for max_n <= 8
-constexpr int kMaxRows = 64;      // depth limit (draft rows)
+constexpr int kMaxTail = 7;        // max_n - 1 for max_n <= 8
+constexpr int kMaxRows = 64;       // depth limit (draft rows)
 constexpr int kMaxBudget = 1024;
 constexpr int kMaxWindow = 8192;
+constexpr int kMaxHashSlots = 32768;
+constexpr uint32_t kEmpty = 0xFFFFFFFFu;
+constexpr uint32_t kNoCand = 0xFFFFFFFFu;
 
 struct BuildArgs {
   const float* lp;
@@ -34,6 +42,9 @@ struct BuildArgs {
   double max_bonus;
   const double* log1p_table;
   int table_len;
+  int hash_slots;    // power of two (>= 64) when there is an n-gram table, else 0
+  int stage_topk;    // top-k staged in shared memory
+  int mask_in_smem;  // ancestor rows kept in shared memory
   int64_t* node_tokens;
   int64_t* node_depths;
   int32_t* parents;
@@ -49,287 +60,340 @@ struct BuildArgs {
   int* status;
 };
 
-struct Frontier {
-  double* aug;
-  double* logw;
-  double* bonus;
-  double* inc;
-  int* parent;  // -1 once popped
-  int* rank;
-  int* depth;
+// ---------------------------------------------------------------------------
+// n-gram hash table: slot = [count:16][order-2:3][window position:13]
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t mix32(uint32_t h) {
+  h ^= h >> 16;
+  h *= 0x7FEB352Du;
+  h ^= h >> 15;
+  h *= 0x846CA68Bu;
+  h ^= h >> 16;
+  return h;
+}
+
+// hash of n = p+1 tokens: p prefix tokens then `next`
+__device__ __forceinline__ uint32_t ngram_hash(const int* prefix, int p, int next) {
+  uint32_t h = 0x811C9DC5u ^ static_cast<uint32_t>(p);
+  for (int q = 0; q < p; ++q) h = (h ^ static_cast<uint32_t>(prefix[q])) * 0x01000193u;
+  h = (h ^ static_cast<uint32_t>(next)) * 0x01000193u;
+  return mix32(h);
+}
+
+__device__ __forceinline__ bool ngram_at(const int* ctx, int pos, const int* prefix, int p, int next) {
+  for (int q = 0; q < p; ++q)
+    if (ctx[pos + q] != prefix[q]) return false;
+  return ctx[pos + p] == next;
+}
+
+// Count the n-gram starting at window position i (prefix length p).
+__device__ void ngram_insert(uint32_t* table, int mask, const int* ctx, int i, int p) {
+  const int* pre = ctx + i;
+  const int next = ctx[i + p];
+  uint32_t s = ngram_hash(pre, p, next) & static_cast<uint32_t>(mask);
+  const uint32_t mine = (1u << 16) | (static_cast<uint32_t>(p - 1) << 13) | static_cast<uint32_t>(i);
+  for (int probe = 0; probe <= mask; ++probe) {
+    uint32_t cur = table[s];
+    if (cur == kEmpty) {
+      cur = atomicCAS(&table[s], kEmpty, mine);
+      if (cur == kEmpty) return;
+    }
+    if (((cur >> 13) & 7u) == static_cast<uint32_t>(p - 1) && ngram_at(ctx, cur & 0x1FFFu, pre, p, next)) {
+      atomicAdd(&table[s], 1u << 16);
+      return;
+    }
+    s = (s + 1) & static_cast<uint32_t>(mask);
+  }
+}
+
+// Occurrences of (tail[tail_len-p .. tail_len), token) in the window.
+__device__ int ngram_count(const uint32_t* table, int mask, const int* ctx, const int* tail, int tail_len, int p,
+                           int token) {
+  const int* pre = tail + (tail_len - p);
+  uint32_t s = ngram_hash(pre, p, token) & static_cast<uint32_t>(mask);
+  for (int probe = 0; probe <= mask; ++probe) {
+    const uint32_t cur = table[s];
+    if (cur == kEmpty) return 0;
+    if (((cur >> 13) & 7u) == static_cast<uint32_t>(p - 1) && ngram_at(ctx, cur & 0x1FFFu, pre, p, token))
+      return static_cast<int>(cur >> 16);
+    s = (s + 1) & static_cast<uint32_t>(mask);
+  }
+  return 0;
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory layout (identical on host and device)
+// ---------------------------------------------------------------------------
+struct Layout {
+  size_t f_aug, f_logw, f_bonus, f_inc, f_tok, f_parent, f_rank, f_depth;
+  size_t n_tail, n_rank, n_depth, n_parent, n_mask;
+  size_t ctx, table, s_lp, s_ids, total;
 };
 
-struct Nodes {
-  int* tail;   // [nn][8]: tokens then length in slot 7
-  int* rank;
-  int* depth;
-  int* parent;
-};
+__host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
 
-// Candidate comparison key carried through the warp arg-max.
-struct Key {
-  double score;
-  int parent, rank, depth, slot;
-};
-
-__device__ __forceinline__ Key shfl_key(const Key& a, int src_lane_xor) {
-  Key b;
-  b.score = __shfl_xor_sync(0xFFFFFFFFu, a.score, src_lane_xor);
-  b.parent = __shfl_xor_sync(0xFFFFFFFFu, a.parent, src_lane_xor);
-  b.rank = __shfl_xor_sync(0xFFFFFFFFu, a.rank, src_lane_xor);
-  b.depth = __shfl_xor_sync(0xFFFFFFFFu, a.depth, src_lane_xor);
-  b.slot = __shfl_xor_sync(0xFFFFFFFFu, a.slot, src_lane_xor);
-  return b;
+__host__ __device__ inline Layout make_layout(int budget, int win, int hash_slots, int rows, int k, int words,
+                                              bool stage, bool mask_smem) {
+  Layout L{};
+  const size_t FC = static_cast<size_t>(budget) + 2, NN = static_cast<size_t>(budget) + 1;
+  size_t o = 0;
+  auto put = [&](size_t bytes) {
+    const size_t at = o;
+    o += al16(bytes);
+    return at;
+  };
+  L.f_aug = put(8 * FC);
+  L.f_logw = put(8 * FC);
+  L.f_bonus = put(8 * FC);
+  L.f_inc = put(8 * FC);
+  L.f_tok = put(8 * FC);
+  L.f_parent = put(4 * FC);
+  L.f_rank = put(4 * FC);
+  L.f_depth = put(4 * FC);
+  L.n_tail = put(32 * NN);
+  L.n_rank = put(4 * NN);
+  L.n_depth = put(4 * NN);
+  L.n_parent = put(4 * NN);
+  L.n_mask = mask_smem ? put(4 * NN * static_cast<size_t>(words)) : 0;
+  L.ctx = put(4 * static_cast<size_t>(win > 0 ? win : 1));
+  L.table = put(4 * static_cast<size_t>(hash_slots > 0 ? hash_slots : 1));
+  L.s_lp = stage ? put(4 * static_cast<size_t>(rows) * k) : 0;
+  L.s_ids = stage ? put(8 * static_cast<size_t>(rows) * k) : 0;
+  L.total = o;
+  return L;
 }
 
 // Rank path of a candidate (parent node p, own rank r, depth d): the ranks of
 // its ancestors at depths 1..d-1 followed by r -- the tuple the original heap
 // compares after the score (ddtree.py:241-243, :265, :284).
-__device__ bool path_less(const Nodes& nd, const Key& a, const Key& b) {
+__device__ bool path_less(const int* nrank, const int* nparent, int pa_node, int ra, int da, int pb_node, int rb,
+                          int db) {
   int pa[kMaxRows + 1], pb[kMaxRows + 1];
-  pa[a.depth] = a.rank;
-  for (int t = a.depth - 1, node = a.parent; t >= 1; --t) {
-    pa[t] = nd.rank[node];
-    node = nd.parent[node];
+  pa[da] = ra;
+  for (int t = da - 1, node = pa_node; t >= 1; --t) {
+    pa[t] = nrank[node];
+    node = nparent[node];
   }
-  pb[b.depth] = b.rank;
-  for (int t = b.depth - 1, node = b.parent; t >= 1; --t) {
-    pb[t] = nd.rank[node];
-    node = nd.parent[node];
+  pb[db] = rb;
+  for (int t = db - 1, node = pb_node; t >= 1; --t) {
+    pb[t] = nrank[node];
+    node = nparent[node];
   }
-  const int m = min(a.depth, b.depth);
+  const int m = min(da, db);
   for (int t = 1; t <= m; ++t)
     if (pa[t] != pb[t]) return pa[t] < pb[t];
-  return a.depth < b.depth;
-}
-
-// True if candidate a is popped before b.  slot < 0 marks "no candidate".
-__device__ __forceinline__ bool better(const Nodes& nd, bool heap_order, const Key& a, const Key& b) {
-  if (a.slot < 0) return false;
-  if (b.slot < 0) return true;
-  if (a.score != b.score) return a.score > b.score;
-  if (heap_order) return path_less(nd, a, b);
-  if (a.parent != b.parent) return a.parent < b.parent;  // ddtree.py:432-434 tuple order
-  return a.rank < b.rank;
-}
-
-struct Ngram {
-  const int* ctx;                        // window, shared memory
-  const unsigned long long* pairs;       // sorted (token << 32 | position), shared memory
-  int len;                               // window length
-  int npairs;                            // len - 1
-};
-
-// First index in pairs[0..n) whose value >= target (warp-cooperative).
-__device__ __forceinline__ int warp_lower_bound(const unsigned long long* pairs, int n, unsigned long long target) {
-  const int lane = threadIdx.x & 31;
-  int lo = 0, hi = n;
-  while (hi - lo > 31) {
-    const int step = (hi - lo + 31) >> 5;
-    const int p = lo + lane * step;
-    const bool pred = (p >= hi) || (pairs[p] >= target);
-    const unsigned b = __ballot_sync(0xFFFFFFFFu, pred);
-    if (b == 0u) {
-      lo = lo + 31 * step + 1;
-      continue;
-    }
-    const int f = __ffs(b) - 1;
-    if (f == 0) return lo;
-    const int nlo = lo + (f - 1) * step + 1;
-    hi = min(hi, lo + f * step);
-    lo = nlo;
-  }
-  const int p = lo + lane;
-  const bool pred = (p >= hi) || (pairs[p] >= target);
-  const unsigned b = __ballot_sync(0xFFFFFFFFu, pred);
-  return lo + __ffs(b) - 1;
-}
-
-// Continuity bonus of appending `token` after `tail` (ddtree.py:154-186),
-// computed by warp 0; every lane returns the same value.
-__device__ double ngram_bonus(const BuildArgs& a, const Ngram& g, const int* tail, int tail_len, int64_t token) {
-  if (g.len < 2) return 0.0;  // empty table (ddtree.py:165)
-  const int lane = threadIdx.x & 31;
-  const unsigned long long t = static_cast<unsigned long long>(token);
-  const int lo = warp_lower_bound(g.pairs, g.npairs, t << 32);
-  const int hi = warp_lower_bound(g.pairs, g.npairs, (t + 1) << 32);
-  const int maxp = min(a.max_n - 1, tail_len);
-  int cnt[kMaxTail];
-#pragma unroll
-  for (int p = 0; p < kMaxTail; ++p) cnt[p] = 0;
-  for (int i = lo + lane; i < hi; i += 32) {
-    const int j = static_cast<int>(g.pairs[i] & 0xFFFFFFFFull);
-    int m = 0;
-    while (m < maxp && m < j && g.ctx[j - 1 - m] == tail[tail_len - 1 - m]) ++m;
-#pragma unroll
-    for (int p = 0; p < kMaxTail; ++p) cnt[p] += (m >= p + 1);
-  }
-  double total = 0.0;
-  for (int n = 2; n <= a.max_n; ++n) {
-    const int p = n - 1;
-    const int c = __reduce_add_sync(0xFFFFFFFFu, cnt[p - 1]);
-    if (tail_len < p) continue;
-    if (c < a.min_count) continue;
-    const double base = a.use_log_count ? a.log1p_table[min(c, a.table_len - 1)] : 1.0;
-    total = __dadd_rn(total, __dmul_rn(a.ow[n - 2], base));
-  }
-  if (a.max_bonus > 0.0) total = (a.max_bonus < total) ? a.max_bonus : total;
-  return total;
-}
-
-// beta * bonus, gated by rank for the rank-gated strategy (ddtree.py:412-420).
-__device__ __forceinline__ double weighted_inc(const BuildArgs& a, const Ngram& g, const int* tail, int tail_len,
-                                               int64_t token, int rank) {
-  if (a.strategy == 2 && rank > a.rank_cap) return 0.0;
-  const double b = ngram_bonus(a, g, tail, tail_len, token);
-  if (b <= 0.0) return 0.0;
-  return __dmul_rn(a.beta, b);
+  return da < db;
 }
 
 __global__ void __launch_bounds__(kBuildThreads) tree_build_kernel(BuildArgs a) {
   extern __shared__ __align__(16) unsigned char smem[];
   const int tid = threadIdx.x, lane = tid & 31;
-  const int B = a.budget, FC = 2 * B + 2, NN = B + 1;
-  // ---- shared-memory carve-up (must match tree_build_smem) ----
-  size_t off = 0;
-  auto take = [&](size_t bytes) {
-    unsigned char* p = smem + off;
-    off += (bytes + 15) & ~static_cast<size_t>(15);
-    return p;
-  };
-  Frontier f;
-  f.aug = reinterpret_cast<double*>(take(sizeof(double) * FC));
-  f.logw = reinterpret_cast<double*>(take(sizeof(double) * FC));
-  f.bonus = reinterpret_cast<double*>(take(sizeof(double) * FC));
-  f.inc = reinterpret_cast<double*>(take(sizeof(double) * FC));
-  f.parent = reinterpret_cast<int*>(take(sizeof(int) * FC));
-  f.rank = reinterpret_cast<int*>(take(sizeof(int) * FC));
-  f.depth = reinterpret_cast<int*>(take(sizeof(int) * FC));
-  Nodes nd;
-  nd.tail = reinterpret_cast<int*>(take(sizeof(int) * 8 * NN));
-  nd.rank = reinterpret_cast<int*>(take(sizeof(int) * NN));
-  nd.depth = reinterpret_cast<int*>(take(sizeof(int) * NN));
-  nd.parent = reinterpret_cast<int*>(take(sizeof(int) * NN));
+  const int B = a.budget;
   const bool use_ngram = a.strategy != 0;
+
+  // ---- context window (ddtree.py:127-138) ----
   int win = 0;
-  int64_t L = 0;
+  int64_t Lctx = 0;
   const int64_t* ctx_src = nullptr;
   if (a.ctx != nullptr) {
-    L = a.ctx_len_dev != nullptr ? a.ctx_len_dev[0] + a.ctx_len : a.ctx_len;
-    L = L > 0 ? L : 0;
+    Lctx = a.ctx_len_dev != nullptr ? a.ctx_len_dev[0] + a.ctx_len : a.ctx_len;
+    Lctx = Lctx > 0 ? Lctx : 0;
   }
-  if (use_ngram && L > 0) {
-    // the window of ddtree.py:135-136, bounded by the shared memory sized on the host
-    const int64_t w = (a.ctx_window > 0 && L > a.ctx_window) ? a.ctx_window : L;
+  if (use_ngram && Lctx > 0) {
+    const int64_t w = (a.ctx_window > 0 && Lctx > a.ctx_window) ? a.ctx_window : Lctx;
     win = static_cast<int>(w < a.win_cap ? w : static_cast<int64_t>(a.win_cap));
     if (w > a.win_cap && tid == 0) set_status(a.status, RT_DEV_OVERFLOW);
-    ctx_src = a.ctx + (L - win);
+    ctx_src = a.ctx + (Lctx - win);
   }
-  int sort_len = 1;
-  while (sort_len < max(win - 1, 1)) sort_len <<= 1;
-  int* ctx = reinterpret_cast<int*>(take(sizeof(int) * max(win, 1)));
-  unsigned long long* pairs = reinterpret_cast<unsigned long long*>(take(sizeof(unsigned long long) * sort_len));
+  const Layout Ly = make_layout(B, a.win_cap, a.hash_slots, a.rows, a.k, a.mask_words, a.stage_topk != 0,
+                                a.mask_in_smem != 0);
+  double* f_aug = reinterpret_cast<double*>(smem + Ly.f_aug);
+  double* f_logw = reinterpret_cast<double*>(smem + Ly.f_logw);
+  double* f_bonus = reinterpret_cast<double*>(smem + Ly.f_bonus);
+  double* f_inc = reinterpret_cast<double*>(smem + Ly.f_inc);
+  int64_t* f_tok = reinterpret_cast<int64_t*>(smem + Ly.f_tok);
+  int* f_parent = reinterpret_cast<int*>(smem + Ly.f_parent);
+  int* f_rank = reinterpret_cast<int*>(smem + Ly.f_rank);
+  int* f_depth = reinterpret_cast<int*>(smem + Ly.f_depth);
+  int* n_tail = reinterpret_cast<int*>(smem + Ly.n_tail);  // [node][8]: tokens, length in slot 7
+  int* n_rank = reinterpret_cast<int*>(smem + Ly.n_rank);
+  int* n_depth = reinterpret_cast<int*>(smem + Ly.n_depth);
+  int* n_parent = reinterpret_cast<int*>(smem + Ly.n_parent);
+  const int W = a.mask_words;
+  uint32_t* rows_mask = a.mask_in_smem ? reinterpret_cast<uint32_t*>(smem + Ly.n_mask) : a.mask;
+  int* ctx = reinterpret_cast<int*>(smem + Ly.ctx);
+  uint32_t* table = reinterpret_cast<uint32_t*>(smem + Ly.table);
+  const float* lp = a.stage_topk ? reinterpret_cast<const float*>(smem + Ly.s_lp) : a.lp;
+  const int64_t* ids = a.stage_topk ? reinterpret_cast<const int64_t*>(smem + Ly.s_ids) : a.ids;
 
-  // ---- prologue: context window and sorted (token, next-position) pairs ----
+  // ---- prologue: window, n-gram counts, staged top-k ----
+  const int hmask = a.hash_slots - 1;
   for (int i = tid; i < win; i += kBuildThreads) ctx[i] = static_cast<int>(ctx_src[i]);
-  __syncthreads();
-  for (int i = tid; i < sort_len; i += kBuildThreads) {
-    const int j = i + 1;  // "next" positions 1..win-1
-    pairs[i] = j < win ? ((static_cast<unsigned long long>(static_cast<uint32_t>(ctx[j])) << 32) | static_cast<uint32_t>(j))
-                       : ~0ull;
-  }
-  __syncthreads();
-  for (int size = 2; size <= sort_len; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < sort_len; i += kBuildThreads) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool asc = (i & size) == 0;
-          const unsigned long long x = pairs[i], y = pairs[j];
-          if (asc ? (x > y) : (x < y)) {
-            pairs[i] = y;
-            pairs[j] = x;
-          }
-        }
-      }
-      __syncthreads();
+  for (int i = tid; i < a.hash_slots; i += kBuildThreads) table[i] = kEmpty;
+  if (a.stage_topk) {
+    float* slp = reinterpret_cast<float*>(smem + Ly.s_lp);
+    int64_t* sids = reinterpret_cast<int64_t*>(smem + Ly.s_ids);
+    for (int i = tid; i < a.rows * a.k; i += kBuildThreads) {
+      slp[i] = a.lp[i];
+      sids[i] = a.ids[i];
     }
   }
+  __syncthreads();
+  // the table of ddtree.py:141-149: for n in 2..max_n, every window position i < win-(n-1)
+  const bool have_table = use_ngram && win >= 2 && a.hash_slots > 0;  // else the table is empty (:165)
+  if (have_table) {
+    for (int p = 1; p <= a.max_n - 1; ++p)
+      for (int i = tid; i < win - p; i += kBuildThreads) ngram_insert(table, hmask, ctx, i, p);
+  }
+  __syncthreads();
   if (tid >= 32) return;
 
   // ---- expansion (warp 0) ----
-  Ngram g{ctx, pairs, win, max(win - 1, 0)};
   const int tail_size = a.max_n - 1;
   const bool heap_order = a.strategy == 0;
+  const bool gated = a.strategy == 2;
   int64_t root = a.root_dev != nullptr ? a.root_dev[0] : a.root;
-  if (a.root_dev == nullptr && a.root < 0) root = L > 0 ? a.ctx[L - 1] : 0;
+  if (a.root_dev == nullptr && a.root < 0) root = Lctx > 0 ? a.ctx[Lctx - 1] : 0;
   const int64_t start = a.start_dev != nullptr ? a.start_dev[0] : a.start;
-  const int W = a.mask_words;
-  // root node 0: tail = last tail_size window ids; mask row 0 = {0}
   if (lane == 0) {
-    int tl = use_ngram ? min(tail_size, win) : 0;
-    for (int q = 0; q < tl; ++q) nd.tail[q] = ctx[win - tl + q];
-    nd.tail[7] = tl;
-    nd.rank[0] = 0;
-    nd.depth[0] = 0;
-    nd.parent[0] = -1;
+    const int tl = use_ngram ? min(tail_size, win) : 0;  // initial tail = last ids of the window
+    for (int q = 0; q < tl; ++q) n_tail[q] = ctx[win - tl + q];
+    n_tail[7] = tl;
+    n_rank[0] = 0;
+    n_depth[0] = 0;
+    n_parent[0] = -1;
     a.parents[0] = -1;
     if (a.verify_ids) a.verify_ids[0] = root;
     if (a.verify_pos) a.verify_pos[0] = start;
   }
-  for (int w = lane; w < W; w += 32) a.mask[w] = (w == 0) ? 1u : 0u;
+  for (int w = lane; w < W; w += 32) {
+    const uint32_t v = (w == 0) ? 1u : 0u;
+    rows_mask[w] = v;
+    if (a.mask_in_smem) a.mask[w] = v;
+  }
   __syncwarp();
+
+  // beta * min(sum_n w^(n-2) * log1p(count_n), cap) of up to two queries at once
+  // (ddtree.py:154-186, :412-420): query 0 on lanes 0..15 (one lane per order),
+  // query 1 on lanes 16..31; every lane returns both results.
+  auto bonus_pair = [&](const int* t0, int64_t tok0, bool on0, const int* t1, int64_t tok1, bool on1,
+                        double& inc0, double& inc1) {
+    const bool q1 = lane >= 16;
+    const int* tl_ptr = q1 ? t1 : t0;
+    const int p = (lane & 15) + 1;
+    int c = 0;
+    if ((q1 ? on1 : on0) && p <= tail_size && p <= tl_ptr[7])
+      c = ngram_count(table, hmask, ctx, tl_ptr, tl_ptr[7], p, static_cast<int>(q1 ? tok1 : tok0));
+    // each lane fetches its own order's log1p(count), so the loads overlap
+    const double base = a.use_log_count ? a.log1p_table[min(c, a.table_len - 1)] : 1.0;
+    const int tla = t0[7], tlb = t1[7];
+    double sa = 0.0, sb = 0.0;
+    for (int n = 2; n <= a.max_n; ++n) {
+      const int ca = __shfl_sync(0xFFFFFFFFu, c, n - 2);
+      const int cb = __shfl_sync(0xFFFFFFFFu, c, 16 + n - 2);
+      const double ba = __shfl_sync(0xFFFFFFFFu, base, n - 2);
+      const double bb = __shfl_sync(0xFFFFFFFFu, base, 16 + n - 2);
+      if (tla >= n - 1 && ca >= a.min_count) sa = __dadd_rn(sa, __dmul_rn(a.ow[n - 2], ba));
+      if (tlb >= n - 1 && cb >= a.min_count) sb = __dadd_rn(sb, __dmul_rn(a.ow[n - 2], bb));
+    }
+    if (a.max_bonus > 0.0) {
+      sa = (a.max_bonus < sa) ? a.max_bonus : sa;
+      sb = (a.max_bonus < sb) ? a.max_bonus : sb;
+    }
+    inc0 = (!on0 || sa <= 0.0) ? 0.0 : __dmul_rn(a.beta, sa);
+    inc1 = (!on1 || sb <= 0.0) ? 0.0 : __dmul_rn(a.beta, sb);
+  };
+
   int nfront = 0, count = 0;
   if (B > 0 && a.rows > 0) {
-    const int64_t tok0 = a.ids[0];
-    const double w0 = static_cast<double>(a.lp[0]);
-    double b0 = 0.0;
-    if (use_ngram) b0 = weighted_inc(a, g, nd.tail, nd.tail[7], tok0, 0);
+    const int64_t tok0 = ids[0];
+    const double w0 = static_cast<double>(lp[0]);
+    double b0 = 0.0, unused = 0.0;
+    if (use_ngram) bonus_pair(n_tail, tok0, have_table && !(gated && 0 > a.rank_cap), n_tail, 0, false, b0, unused);
     if (lane == 0) {
-      f.aug[0] = __dadd_rn(w0, b0);
-      f.logw[0] = w0;
-      f.bonus[0] = b0;
-      f.inc[0] = b0;
-      f.parent[0] = 0;
-      f.rank[0] = 0;
-      f.depth[0] = 1;
+      f_aug[0] = __dadd_rn(w0, b0);
+      f_logw[0] = w0;
+      f_bonus[0] = b0;
+      f_inc[0] = b0;
+      f_tok[0] = tok0;
+      f_parent[0] = 0;
+      f_rank[0] = 0;
+      f_depth[0] = 1;
     }
     nfront = 1;
     __syncwarp();
   }
   while (count < B && nfront > 0) {
-    // arg-max over the live frontier
-    Key best{0.0, 0, 0, 0, -1};
+    // ---- arg-max: (score desc, then the heap tuple's tie order) ----
+    double bs = -INFINITY;
+    uint32_t bk = kNoCand;  // (parent << 21) | (rank << 11) | slot
     for (int e = lane; e < nfront; e += 32) {
-      if (f.parent[e] < 0) continue;
-      Key c{f.aug[e], f.parent[e], f.rank[e], f.depth[e], e};
-      if (better(nd, heap_order, c, best)) best = c;
+      const double s = f_aug[e];
+      const uint32_t key = (static_cast<uint32_t>(f_parent[e]) << 21) | (static_cast<uint32_t>(f_rank[e]) << 11) |
+                           static_cast<uint32_t>(e);
+      bool take = bk == kNoCand || s > bs;
+      if (!take && s == bs) {
+        if (heap_order) {
+          const int eb = bk & 0x7FF;
+          take = path_less(n_rank, n_parent, f_parent[e], f_rank[e], f_depth[e], f_parent[eb], f_rank[eb],
+                           f_depth[eb]);
+        } else {
+          take = key < bk;
+        }
+      }
+      if (take) {
+        bs = s;
+        bk = key;
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const Key other = shfl_key(best, o);
-      if (better(nd, heap_order, other, best)) best = other;
+      const double os = __shfl_xor_sync(0xFFFFFFFFu, bs, o);
+      const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
+      bool take = ok != kNoCand && (bk == kNoCand || os > bs);
+      if (!take && ok != kNoCand && os == bs) {
+        if (heap_order) {
+          const int ea = ok & 0x7FF, eb = bk & 0x7FF;
+          take = path_less(n_rank, n_parent, f_parent[ea], f_rank[ea], f_depth[ea], f_parent[eb], f_rank[eb],
+                           f_depth[eb]);
+        } else {
+          take = ok < bk;
+        }
+      }
+      if (take) {
+        bs = os;
+        bk = ok;
+      }
     }
-    if (best.slot < 0) break;  // frontier empty
-    const int e = best.slot;
-    const int parent = best.parent, rank = best.rank, depth = best.depth;
-    const double logw = f.logw[e], bonus = f.bonus[e], inc_self = f.inc[e];
+    if (bk == kNoCand) break;
+    const int e = static_cast<int>(bk & 0x7FF);
+    const int parent = static_cast<int>(bk >> 21), rank = static_cast<int>((bk >> 11) & 0x3FF);
+    const int depth = f_depth[e];
+    const double logw = f_logw[e], bonus = f_bonus[e], inc_self = f_inc[e];
+    const int64_t tok = f_tok[e];
     const int me = count + 1;
-    const int64_t tok = a.ids[static_cast<int64_t>(depth - 1) * a.k + rank];
+    // operands of the two pushes
+    const int64_t row = static_cast<int64_t>(depth - 1) * a.k;
+    const bool has_sib = rank + 1 < a.k;
+    const bool has_child = depth < a.rows;
+    const float lp_cur = lp[row + rank];
+    const float lp_sib = has_sib ? lp[row + rank + 1] : 0.f;
+    const int64_t tok_sib = has_sib ? ids[row + rank + 1] : 0;
+    const float lp_child = has_child ? lp[row + a.k] : 0.f;
+    const int64_t tok_child = has_child ? ids[row + a.k] : 0;
     __syncwarp();
     if (lane == 0) {
-      f.parent[e] = -1;
+      // emit node `me`; the frontier's last entry fills the popped slot
       a.node_tokens[count] = tok;
       a.node_depths[count] = depth;
       a.parents[me] = parent;
       if (a.verify_ids) a.verify_ids[me] = tok;
       if (a.verify_pos) a.verify_pos[me] = start + depth;
-      nd.rank[me] = rank;
-      nd.depth[me] = depth;
-      nd.parent[me] = parent;
-      // own tail = parent's tail + token, keeping the last tail_size ids
-      const int* pt = nd.tail + 8 * parent;
-      int* mt = nd.tail + 8 * me;
+      n_rank[me] = rank;
+      n_depth[me] = depth;
+      n_parent[me] = parent;
+      const int* pt = n_tail + 8 * parent;  // own tail = parent's tail + token, last tail_size ids
+      int* mt = n_tail + 8 * me;
       const int pl = pt[7];
       if (pl < tail_size) {
         for (int q = 0; q < pl; ++q) mt[q] = pt[q];
@@ -340,77 +404,67 @@ __global__ void __launch_bounds__(kBuildThreads) tree_build_kernel(BuildArgs a) 
         if (tail_size > 0) mt[tail_size - 1] = static_cast<int>(tok);
         mt[7] = tail_size;
       }
+      const int last = nfront - 1;
+      if (e != last) {
+        f_aug[e] = f_aug[last];
+        f_logw[e] = f_logw[last];
+        f_bonus[e] = f_bonus[last];
+        f_inc[e] = f_inc[last];
+        f_tok[e] = f_tok[last];
+        f_parent[e] = f_parent[last];
+        f_rank[e] = f_rank[last];
+        f_depth[e] = f_depth[last];
+      }
     }
-    // ancestor mask row = parent's row | own bit
+    // ancestor row = parent's row | own bit (visibility of ddtree.py:520-528)
     for (int w = lane; w < W; w += 32) {
-      uint32_t v = a.mask[static_cast<int64_t>(parent) * W + w];
+      uint32_t v = rows_mask[static_cast<int64_t>(parent) * W + w];
       if (w == (me >> 5)) v |= 1u << (me & 31);
-      a.mask[static_cast<int64_t>(me) * W + w] = v;
+      rows_mask[static_cast<int64_t>(me) * W + w] = v;
+      if (a.mask_in_smem) a.mask[static_cast<int64_t>(me) * W + w] = v;
     }
-    __syncwarp();
+    --nfront;
     count = me;
-    // sibling: next rank in the same row (ddtree.py:464-490 / :264-281)
-    if (rank + 1 < a.k) {
-      const int r2 = rank + 1;
-      const int64_t row = static_cast<int64_t>(depth - 1) * a.k;
-      const double w2 = __dadd_rn(__dsub_rn(logw, static_cast<double>(a.lp[row + rank])),
-                                  static_cast<double>(a.lp[row + r2]));
-      double inc2 = 0.0, b2 = 0.0;
-      if (use_ngram) {
-        const int* pt = nd.tail + 8 * parent;
-        inc2 = weighted_inc(a, g, pt, pt[7], a.ids[row + r2], r2);
-        b2 = __dadd_rn(__dsub_rn(bonus, inc_self), inc2);
-      }
-      if (lane == 0) {
-        f.aug[nfront] = use_ngram ? __dadd_rn(w2, b2) : w2;
-        f.logw[nfront] = w2;
-        f.bonus[nfront] = b2;
-        f.inc[nfront] = inc2;
-        f.parent[nfront] = parent;
-        f.rank[nfront] = r2;
-        f.depth[nfront] = depth;
-      }
-      ++nfront;
-    }
-    // first child: rank 0 of the next row (ddtree.py:492-516 / :283-289)
-    if (depth < a.rows) {
-      const int64_t row = static_cast<int64_t>(depth) * a.k;
-      const double w2 = __dadd_rn(logw, static_cast<double>(a.lp[row]));
-      double inc2 = 0.0, b2 = 0.0;
-      if (use_ngram) {
-        __syncwarp();
-        const int* mt = nd.tail + 8 * me;
-        inc2 = weighted_inc(a, g, mt, mt[7], a.ids[row], 0);
-        b2 = __dadd_rn(bonus, inc2);
-      }
-      if (lane == 0) {
-        f.aug[nfront] = use_ngram ? __dadd_rn(w2, b2) : w2;
-        f.logw[nfront] = w2;
-        f.bonus[nfront] = b2;
-        f.inc[nfront] = inc2;
-        f.parent[nfront] = me;
-        f.rank[nfront] = 0;
-        f.depth[nfront] = depth + 1;
-      }
-      ++nfront;
-    }
     __syncwarp();
-    if (nfront > FC) {
-      if (lane == 0) set_status(a.status, RT_DEV_OVERFLOW);
-      break;
+    // bonuses of both pushes at once: the sibling's tail is the parent's, the child's is `me`'s
+    double inc_sib = 0.0, inc_child = 0.0;
+    if (use_ngram && (has_sib || has_child)) {
+      const bool on_sib = has_sib && have_table && !(gated && rank + 1 > a.rank_cap);
+      const bool on_child = has_child && have_table && !(gated && 0 > a.rank_cap);
+      bonus_pair(n_tail + 8 * parent, tok_sib, on_sib, n_tail + 8 * me, tok_child, on_child, inc_sib, inc_child);
     }
+    if (lane == 0) {
+      if (has_sib) {  // next rank in the same row (ddtree.py:464-490 / :264-281)
+        const double w2 = __dadd_rn(__dsub_rn(logw, static_cast<double>(lp_cur)), static_cast<double>(lp_sib));
+        const double b2 = use_ngram ? __dadd_rn(__dsub_rn(bonus, inc_self), inc_sib) : 0.0;
+        const int s = nfront;
+        f_aug[s] = use_ngram ? __dadd_rn(w2, b2) : w2;
+        f_logw[s] = w2;
+        f_bonus[s] = b2;
+        f_inc[s] = inc_sib;
+        f_tok[s] = tok_sib;
+        f_parent[s] = parent;
+        f_rank[s] = rank + 1;
+        f_depth[s] = depth;
+      }
+      if (has_child) {  // rank 0 of the next row (ddtree.py:492-516 / :283-289)
+        const double w2 = __dadd_rn(logw, static_cast<double>(lp_child));
+        const double b2 = use_ngram ? __dadd_rn(bonus, inc_child) : 0.0;
+        const int s = nfront + static_cast<int>(has_sib);
+        f_aug[s] = use_ngram ? __dadd_rn(w2, b2) : w2;
+        f_logw[s] = w2;
+        f_bonus[s] = b2;
+        f_inc[s] = inc_child;
+        f_tok[s] = tok_child;
+        f_parent[s] = me;
+        f_rank[s] = 0;
+        f_depth[s] = depth + 1;
+      }
+    }
+    nfront += static_cast<int>(has_sib) + static_cast<int>(has_child);
+    __syncwarp();
   }
   if (lane == 0) *a.count_out = count;
-}
-
-static size_t tree_build_smem(int budget, int win) {
-  const size_t FC = 2 * static_cast<size_t>(budget) + 2, NN = budget + 1;
-  auto al = [](size_t x) { return (x + 15) & ~static_cast<size_t>(15); };
-  size_t s = 4 * al(8 * FC) + 3 * al(4 * FC) + al(32 * NN) + 3 * al(4 * NN);
-  size_t sort_len = 1;
-  while (sort_len < static_cast<size_t>(std::max(win - 1, 1))) sort_len <<= 1;
-  s += al(4 * static_cast<size_t>(std::max(win, 1))) + al(8 * sort_len);
-  return s;
 }
 
 }  // namespace rt
@@ -426,7 +480,7 @@ extern "C" int rt_tree_build(const float* top_logp, const int64_t* top_ids, int 
                              int64_t* verify_pos, int64_t root, const int64_t* root_dev, int64_t start,
                              const int64_t* start_dev, int* status, rt_stream_t stream) {
   if (rows < 0 || k <= 0 || budget < 0 || strategy < 0 || strategy > 2) return RT_ERR_INVALID_ARGUMENT;
-  if (budget > kMaxBudget || rows > kMaxRows) return RT_ERR_UNSUPPORTED;
+  if (budget > kMaxBudget || rows > kMaxRows || k > 1024) return RT_ERR_UNSUPPORTED;
   if (!parents || !mask || !count || !node_tokens || !node_depths) return RT_ERR_INVALID_ARGUMENT;
   if (mask_words < (budget + 1 + 31) / 32) return RT_ERR_INVALID_ARGUMENT;
   if (budget > 0 && rows > 0 && (!top_logp || !top_ids)) return RT_ERR_INVALID_ARGUMENT;
@@ -434,6 +488,7 @@ extern "C" int rt_tree_build(const float* top_logp, const int64_t* top_ids, int 
   if (ctx != nullptr && ctx_len_dev == nullptr && ctx_len < 0) return RT_ERR_INVALID_ARGUMENT;
   // Largest window the kernel may see; shared memory is sized for it.
   int64_t win_cap = 0;
+  int slots = 0;
   if (strategy != 0 && ctx != nullptr) {
     if (ctx_len_dev == nullptr)
       win_cap = ctx_window > 0 ? std::min<int64_t>(ctx_len, ctx_window) : ctx_len;
@@ -442,6 +497,10 @@ extern "C" int rt_tree_build(const float* top_logp, const int64_t* top_ids, int 
     if (win_cap > kMaxWindow) return RT_ERR_UNSUPPORTED;
     if (use_log_count && (log1p_table == nullptr || table_len < win_cap + 1)) return RT_ERR_INVALID_ARGUMENT;
     if (order_weight == nullptr) return RT_ERR_INVALID_ARGUMENT;
+    const int64_t keys = static_cast<int64_t>(max_n - 1) * win_cap;
+    if (keys > (kMaxHashSlots * 4) / 5) return RT_ERR_UNSUPPORTED;  // keep the table under 80 % full
+    slots = 64;
+    while (slots < 2 * keys + 1 && slots < kMaxHashSlots) slots <<= 1;
   }
   BuildArgs a{};
   a.lp = top_logp;
@@ -464,6 +523,7 @@ extern "C" int rt_tree_build(const float* top_logp, const int64_t* top_ids, int 
   a.max_bonus = max_token_bonus;
   a.log1p_table = log1p_table;
   a.table_len = table_len;
+  a.hash_slots = slots;
   a.node_tokens = node_tokens;
   a.node_depths = node_depths;
   a.parents = parents;
@@ -477,8 +537,19 @@ extern "C" int rt_tree_build(const float* top_logp, const int64_t* top_ids, int 
   a.start = start;
   a.start_dev = start_dev;
   a.status = status;
-  const size_t smem = tree_build_smem(budget, static_cast<int>(win_cap));
-  if (smem > 227 * 1024) return RT_ERR_UNSUPPORTED;
+  // optional shared-memory residents: the staged top-k, then the ancestor rows
+  constexpr size_t kSmemBudget = 220 * 1024;
+  const int stage_rows = rows > 0 ? rows : 1;
+  a.mask_in_smem = 1;
+  a.stage_topk = 1;
+  if (make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, true, true).total > kSmemBudget)
+    a.stage_topk = 0;
+  if (make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, a.stage_topk, true).total > kSmemBudget)
+    a.mask_in_smem = 0;
+  const size_t smem =
+      make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, a.stage_topk, a.mask_in_smem).total;
+  if (smem > kSmemBudget) return RT_ERR_UNSUPPORTED;
+  if (rows == 0) a.stage_topk = 0;
   set_smem_limit(tree_build_kernel, smem);
   tree_build_kernel<<<1, kBuildThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return check_launch();
