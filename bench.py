@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--cpu-sample-rounds", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from Python instead of graph replays")
+    ap.add_argument("--hf-forward", action="store_true",
+                    help="run the verify forward through the transformers modules instead of the fused stages")
     return ap.parse_args()
 
 
@@ -204,8 +206,8 @@ def run_ours(args, wl, rank, world, local_rank):
         target = build_target(cfg, device=dev, seed=0, attn_implementation=headsplit.NAME)
         headsplit.shard_attention_heads(target, rank, world)
     else:
-        log(rank, "target built")
-    target = build_target(cfg, device=dev, seed=0)
+        target = build_target(cfg, device=dev, seed=0)
+    log(rank, "target built")
     steps, warm = args.steps, args.warmup
     total_rounds = warm + steps
     max_len = wl["prompt"] + total_rounds * (wl["block"] + 2) + 64
@@ -218,7 +220,8 @@ def run_ours(args, wl, rank, world, local_rank):
     prompt = torch.from_numpy(np.random.default_rng(req).integers(0, cfg.vocab_size, size=wl["prompt"]))[None]
 
     def fresh():
-        v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1)
+        v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
+                         fused=not args.hf_forward)
         if wl.get("split"):
             v.prefill_random(wl["prompt"], seed=req)
         else:
@@ -374,6 +377,7 @@ def run_ours(args, wl, rank, world, local_rank):
                                                       "weights)",
         "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": wl["prompt"],
                    "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
+                   "verify_forward": "transformers modules" if args.hf_forward else "fused stages",
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer)"
                                    if wl.get("split") else f"dp{world} (one request per GPU)" + (
                                        ", recovery-delta all-gather per step" if world > 1 else "")),

@@ -240,6 +240,46 @@ int rt_tree_walk(const int32_t* parents, const int64_t* node_tokens, int count, 
                  const int64_t* verify_ids, int64_t* output_ids, int64_t output_len, int64_t* start_dev,
                  int* status, rt_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Elementwise stages of the target's verify forward (bf16, row-major,
+ * contiguous, 16-byte aligned rows).  Each reproduces the bf16 rounding
+ * points of the transformers ops it replaces; the projections between them
+ * stay library GEMMs.
+ *
+ * rt_embed_rmsnorm: residual[r] = table[ids[r]] (table bf16[vocab, hidden]),
+ *   out[r] = weight * bf16(residual[r] * rsqrt(mean(residual[r]^2) + eps)).
+ *   Replaces the embedding lookup of Qwen3Model.forward plus the first
+ *   Qwen3RMSNorm.forward (models/qwen3/modeling_qwen3.py:59-64).  An id
+ *   outside [0, vocab) gives a zero row and RT_DEV_BAD_INDEX.
+ * rt_add_rmsnorm: residual = bf16(residual + delta) (delta may be NULL: the
+ *   norm of residual alone), out = weight * bf16(norm(residual)).  Replaces
+ *   the residual adds of Qwen3DecoderLayer.forward (modeling_qwen3.py:327,
+ *   :333) with the RMSNorm that follows each.  hidden % 8 == 0, <= 16384.
+ * rt_qk_norm_rope_append: qkv is bf16[n, (Hq + 2 Hkv) * 128] ([q | k | v]
+ *   heads).  Query and key heads get their per-head RMSNorm (weights
+ *   bf16[128]; both NULL for models without one, modeling_qwen3.py:269-270)
+ *   and the rotary embedding with cos/sin rows cos_table[positions[i]]
+ *   (bf16[table_len, 128], :151-181); queries go to q_out bf16[n, Hq, 128],
+ *   keys/values to row offset + i of k_cache/v_cache (+ g*cache_head_stride
+ *   bytes for kv head g, cache_row_stride bytes per row), offset read from
+ *   offset_dev (DEVICE) when non-NULL (cache_utils.py:102-121).  A row
+ *   past `capacity` is not written (RT_DEV_OVERFLOW); a position outside the
+ *   table gives RT_DEV_BAD_INDEX.
+ * rt_silu_mul: out[r] = bf16(bf16(silu(gate)) * up) with gate_up[r] =
+ *   [gate (inter) | up (inter)] (Qwen3MLP.forward, modeling_qwen3.py:81-83).
+ * ---------------------------------------------------------------------- */
+int rt_embed_rmsnorm(const int64_t* ids, const void* table, int64_t vocab, void* residual, const void* weight,
+                     void* out, int rows, int hidden, float eps, int* status, rt_stream_t stream);
+int rt_add_rmsnorm(const void* delta, void* residual, const void* weight, void* out, int rows, int hidden,
+                   float eps, rt_stream_t stream);
+int rt_qk_norm_rope_append(const void* qkv, int n, int num_q_heads, int num_kv_heads, int head_dim,
+                           const void* q_norm_weight, const void* k_norm_weight, float eps, const void* cos_table,
+                           const void* sin_table, int64_t table_len, const int64_t* positions, void* q_out,
+                           void* k_cache, void* v_cache, int64_t cache_head_stride, int64_t cache_row_stride,
+                           int64_t capacity, int64_t offset, const int64_t* offset_dev, int* status,
+                           rt_stream_t stream);
+int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, rt_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,216 @@
+"""The target's tree-verify forward as fused stages over preallocated buffers.
+
+``FusedTarget(model, cache, n_max)`` runs the decoder stack of a
+transformers Qwen3 / Qwen2 / Llama causal LM (pre-norm, rotary, GQA, SiLU
+MLP) for one verify round of ``n <= n_max`` tree nodes without going through
+the module tree.  Per layer the HF forward (models/qwen3/modeling_qwen3.py:
+305-334 with Qwen3Attention.forward :252-299 and Qwen3MLP.forward :81-83)
+issues about forty kernels -- casts, the four RMSNorm steps, rotary slicing
+and concatenation, residual adds, the cache ``torch.cat`` -- around seven
+projections.  Here a layer is nine launches:
+
+  rt_add_rmsnorm          residual += mlp_out; x = rmsnorm(residual) * w_in
+  x @ [Wq;Wk;Wv]^T        one cuBLAS GEMM over the packed projection
+  rt_qk_norm_rope_append  q/k head norms + rotary; q out, k/v into the cache
+  rt_tree_attn            the tree-masked attention kernel
+  attn @ Wo^T             cuBLAS
+  rt_add_rmsnorm          residual += o; x = rmsnorm(residual) * w_post
+  x @ [Wg;Wu]^T           one cuBLAS GEMM over the packed gate/up projection
+  rt_silu_mul             act = silu(gate) * up
+  act @ Wd^T              cuBLAS
+
+and the stack opens with ``rt_embed_rmsnorm`` (embedding lookup + first norm)
+and closes with the final norm and the lm_head GEMM.  The packed projection
+weights are single tensors whose row blocks the HF modules keep as views, so
+the model's memory does not grow and the HF forward stays usable (prefill
+runs through it).
+
+The rotary tables are the model's own ``rotary_emb`` outputs for positions
+``[0, max_positions)`` (bf16, what HF computes per forward), so positions are
+device-side indices.  Numerics follow the HF ops' bf16 rounding points (see
+``csrc/layer_ops.cu``); the projections are the same cuBLAS GEMMs, run over
+the packed weights.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import nn
+
+from . import kernels
+
+SUPPORTED_MODEL_TYPES = ("qwen3", "qwen2", "llama")
+
+
+def supports(model) -> bool:
+    """Whether ``FusedTarget`` can run this model's verify forward."""
+    cfg = model.config
+    if getattr(cfg, "model_type", None) not in SUPPORTED_MODEL_TYPES:
+        return False
+    if getattr(cfg, "hidden_act", "silu") != "silu" or getattr(cfg, "mlp_bias", False):
+        return False
+    hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+    if hd != 128 or cfg.hidden_size % 8 or cfg.intermediate_size % 8:
+        return False
+    if getattr(cfg, "sliding_window", None) and getattr(cfg, "use_sliding_window", False):
+        return False
+    # the rotary tables are precomputed per position: rope types whose
+    # frequencies depend on the sequence length are out
+    for attr in ("rope_parameters", "rope_scaling"):
+        rs = getattr(cfg, attr, None) or {}
+        if isinstance(rs, dict) and rs.get("rope_type", rs.get("type")) in ("dynamic", "longrope"):
+            return False
+    return next(model.parameters()).dtype == torch.bfloat16
+
+
+def _pack(linears) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """One weight (and bias) for several nn.Linear; the modules keep row-block views of it."""
+    w = torch.cat([lin.weight.detach() for lin in linears], dim=0).contiguous()
+    has_bias = [lin.bias is not None for lin in linears]
+    if any(has_bias) and not all(has_bias):
+        raise RuntimeError("packed projections must all have a bias or none")
+    b = torch.cat([lin.bias.detach() for lin in linears]).contiguous() if all(has_bias) else None
+    r = 0
+    for lin in linears:
+        rows = lin.weight.shape[0]
+        lin.weight = nn.Parameter(w[r: r + rows], requires_grad=False)
+        if b is not None:
+            lin.bias = nn.Parameter(b[r: r + rows], requires_grad=False)
+        r += rows
+    return w, b
+
+
+class _Layer:
+    pass
+
+
+class FusedTarget:
+    def __init__(self, model, cache, n_max: int, max_positions: int | None = None):
+        if not supports(model):
+            raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
+        cfg = model.config
+        inner = model.model
+        dev = next(model.parameters()).device
+        self.device = dev
+        self.cache = cache
+        self.n_max = int(n_max)
+        self.head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        self.hidden = cfg.hidden_size
+        self.inter = cfg.intermediate_size
+        self.vocab = cfg.vocab_size
+        self.eps = float(cfg.rms_norm_eps)
+        self.embed = inner.embed_tokens.weight
+        self.final_norm = inner.norm.weight
+        self.lm_head = model.lm_head.weight
+        self.layers = []
+        with torch.no_grad():
+            for i, layer in enumerate(inner.layers):
+                a, m = layer.self_attn, layer.mlp
+                L = _Layer()
+                L.index = i
+                L.in_norm = layer.input_layernorm.weight
+                L.post_norm = layer.post_attention_layernorm.weight
+                L.eps_in = float(getattr(layer.input_layernorm, "variance_epsilon", self.eps))
+                L.eps_post = float(getattr(layer.post_attention_layernorm, "variance_epsilon", self.eps))
+                L.qkv_w, L.qkv_b = _pack([a.q_proj, a.k_proj, a.v_proj])
+                L.gate_up_w, _ = _pack([m.gate_proj, m.up_proj])
+                L.o_w, L.o_b = a.o_proj.weight, a.o_proj.bias
+                L.down_w = m.down_proj.weight
+                L.hq = a.q_proj.weight.shape[0] // self.head_dim
+                L.hkv = a.k_proj.weight.shape[0] // self.head_dim
+                qn, kn = getattr(a, "q_norm", None), getattr(a, "k_norm", None)
+                L.q_norm = None if qn is None else qn.weight
+                L.k_norm = None if kn is None else kn.weight
+                L.eps_qk = float(getattr(qn, "variance_epsilon", self.eps)) if qn is not None else self.eps
+                L.scale = float(getattr(a, "scaling", self.head_dim ** -0.5))
+                L.split = getattr(a, "_rt_head_split", None)
+                self.layers.append(L)
+        hq = self.layers[0].hq
+        hkv = self.layers[0].hkv
+        if cache.num_kv_heads != hkv:
+            raise RuntimeError("cache KV heads do not match the model's (local) KV heads")
+        self.hq, self.hkv = hq, hkv
+        self.max_positions = int(max_positions or cache.capacity)
+        self.cos, self.sin = self._rope_tables(model, self.max_positions)
+        n, d = self.n_max, self.head_dim
+        e = dict(dtype=torch.bfloat16, device=dev)
+        self.residual = torch.empty((n, self.hidden), **e)
+        self.xnorm = torch.empty((n, self.hidden), **e)
+        self.qkv = torch.empty((n, (hq + 2 * hkv) * d), **e)
+        self.q = torch.empty((n, hq, d), **e)
+        self.attn = torch.empty((n, hq, d), **e)
+        self.o = torch.empty((n, self.hidden), **e)
+        self.gate_up = torch.empty((n, 2 * self.inter), **e)
+        self.act = torch.empty((n, self.inter), **e)
+        self.mlp_out = torch.empty((n, self.hidden), **e)
+        self.logits = torch.empty((n, self.vocab), **e)
+
+    @staticmethod
+    def _rope_tables(model, max_positions: int):
+        rot = model.model.rotary_emb
+        dev = next(model.parameters()).device
+        cos_parts, sin_parts = [], []
+        dummy = torch.empty((1, 1), dtype=torch.bfloat16, device=dev)
+        step = 8192
+        with torch.no_grad():
+            for p0 in range(0, max_positions, step):
+                pos = torch.arange(p0, min(max_positions, p0 + step), device=dev).unsqueeze(0)
+                c, s = rot(dummy, pos)
+                cos_parts.append(c[0])
+                sin_parts.append(s[0])
+        return torch.cat(cos_parts).contiguous(), torch.cat(sin_parts).contiguous()
+
+    def _splits(self, n: int) -> int:
+        return kernels.default_splits(n, self.hq, self.hkv, self.cache.capacity - n)
+
+    def _linear(self, x, w, b, out):
+        if b is None:
+            return torch.mm(x, w.t(), out=out)
+        return torch.addmm(b, x, w.t(), out=out)
+
+    @torch.inference_mode()
+    def forward(self, ids: torch.Tensor, positions: torch.Tensor, bits: torch.Tensor, offset: int = 0,
+                offset_dev: torch.Tensor | None = None) -> torch.Tensor:
+        """Logits ``[n, vocab]`` (bf16, a view of a reused buffer) of ``n`` tree nodes.
+
+        ``ids``/``positions``: int64 ``[n]``; ``bits``: int32 ``[n, W]`` ancestor
+        bits of the tree block; K/V rows are appended at ``offset`` (+
+        ``offset_dev[0]``, the device prefix length, when given), and the
+        attention sees every cached row before them.
+        """
+        n = ids.numel()
+        if n > self.n_max:
+            raise RuntimeError(f"{n} nodes exceed the fused forward's n_max {self.n_max}")
+        ids = ids.reshape(n)
+        positions = positions.reshape(n)
+        slab = self.cache.slab
+        cap = self.cache.capacity
+        splits = self._splits(n)
+        res, xn = self.residual[:n], self.xnorm[:n]
+        for L in self.layers:
+            if L.index == 0:
+                kernels.embed_rmsnorm(ids, self.embed, L.in_norm, L.eps_in, res, xn)
+            else:
+                kernels.add_rmsnorm(self.mlp_out[:n], res, L.in_norm, L.eps_in, xn)
+            self._linear(xn, L.qkv_w, L.qkv_b, self.qkv[:n])
+            kc, vc = slab[2 * L.index], slab[2 * L.index + 1]
+            kernels.qk_norm_rope_append(self.qkv[:n], L.hq, L.hkv, L.q_norm, L.k_norm, L.eps_qk, self.cos, self.sin,
+                                        positions, self.q[:n], kc, vc, offset=offset, offset_dev=offset_dev)
+            if offset_dev is not None:
+                kernels.tree_attention(self.q[:n], kc, vc, bits, cap - n, scale=L.scale, out=self.attn[:n],
+                                       num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap)
+            else:
+                kernels.tree_attention(self.q[:n], kc[:, : offset + n], vc[:, : offset + n], bits, offset,
+                                       scale=L.scale, out=self.attn[:n], num_splits=splits, kv_capacity=cap)
+            attn = self.attn[:n]
+            if L.split is not None:
+                from .headsplit import gather_heads
+                group, world, _ = L.split
+                attn = gather_heads(attn.unsqueeze(0), group, world)[0]
+            self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n])
+            kernels.add_rmsnorm(self.o[:n], res, L.post_norm, L.eps_post, xn)
+            torch.mm(xn, L.gate_up_w.t(), out=self.gate_up[:n])
+            kernels.silu_mul(self.gate_up[:n], self.act[:n])
+            torch.mm(self.act[:n], L.down_w.t(), out=self.mlp_out[:n])
+        kernels.add_rmsnorm(self.mlp_out[:n], res, self.final_norm, self.eps, xn)
+        return torch.mm(xn, self.lm_head.t(), out=self.logits[:n])

@@ -350,3 +350,87 @@ def tree_walk(parents: torch.Tensor, tokens: torch.Tensor, posterior: torch.Tens
 
 __all__ = ["kv_compact", "kv_append", "tree_attention", "mask_from_dense", "draft_topk", "tree_build",
            "tree_walk", "log1p_table", "status_tensor", "check_device_status", "STRATEGY_CODE"]
+
+
+# ---------------------------------------------------------------------------
+# Elementwise stages of the verify forward (retree_b200.fused)
+# ---------------------------------------------------------------------------
+def _rows_bf16(t: torch.Tensor, name: str) -> None:
+    if t.dtype != torch.bfloat16 or not t.is_contiguous():
+        raise RuntimeError(f"{name} must be a contiguous bf16 tensor")
+
+
+def embed_rmsnorm(ids: torch.Tensor, table: torch.Tensor, weight: torch.Tensor, eps: float,
+                  residual: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """``residual = table[ids]``; ``out = rmsnorm(residual) * weight`` (bf16, rows = ids.numel())."""
+    _require_cuda(ids, table, weight, residual, out)
+    for t, nm in ((table, "table"), (weight, "weight"), (residual, "residual"), (out, "out")):
+        _rows_bf16(t, nm)
+    if ids.dtype != torch.int64 or not ids.is_contiguous():
+        raise RuntimeError("ids must be contiguous int64")
+    rows, hidden = ids.numel(), table.shape[-1]
+    _lib.check(_lib.load().rt_embed_rmsnorm(ids.data_ptr(), table.data_ptr(), table.shape[0], residual.data_ptr(),
+                                            weight.data_ptr(), out.data_ptr(), rows, hidden, float(eps),
+                                            status_tensor(ids.device).data_ptr(), _stream(ids.device)),
+               "rt_embed_rmsnorm")
+    _count()
+    return out
+
+
+def add_rmsnorm(delta: torch.Tensor | None, residual: torch.Tensor, weight: torch.Tensor, eps: float,
+                out: torch.Tensor) -> torch.Tensor:
+    """``residual += delta`` (bf16 rounding), ``out = rmsnorm(residual) * weight``; delta may be None."""
+    _require_cuda(delta, residual, weight, out)
+    for t, nm in ((residual, "residual"), (weight, "weight"), (out, "out")) + (((delta, "delta"),) if delta is not None else ()):
+        _rows_bf16(t, nm)
+    hidden = residual.shape[-1]
+    rows = residual.numel() // hidden
+    _lib.check(_lib.load().rt_add_rmsnorm(_ptr(delta), residual.data_ptr(), weight.data_ptr(), out.data_ptr(), rows,
+                                          hidden, float(eps), _stream(residual.device)), "rt_add_rmsnorm")
+    _count()
+    return out
+
+
+def qk_norm_rope_append(qkv: torch.Tensor, num_q_heads: int, num_kv_heads: int, q_norm_w, k_norm_w, eps: float,
+                        cos_table: torch.Tensor, sin_table: torch.Tensor, positions: torch.Tensor,
+                        q_out: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, offset: int = 0,
+                        offset_dev: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-head q/k RMSNorm + rotary embedding; q to ``q_out [n, Hq, 128]``, k/v appended to the cache.
+
+    ``k_cache``/``v_cache`` are ``[Hkv, capacity, 128]`` views with unit inner
+    stride; rows land at ``offset`` (+ ``offset_dev[0]`` when given).
+    """
+    _require_cuda(qkv, cos_table, sin_table, positions, q_out, k_cache, v_cache, q_norm_w, k_norm_w, offset_dev)
+    _rows_bf16(qkv, "qkv")
+    _rows_bf16(q_out, "q_out")
+    n = positions.numel()
+    if qkv.numel() != n * (num_q_heads + 2 * num_kv_heads) * 128:
+        raise RuntimeError("qkv does not hold n rows of (Hq + 2 Hkv) heads of 128")
+    if positions.dtype != torch.int64 or not positions.is_contiguous():
+        raise RuntimeError("positions must be contiguous int64")
+    if k_cache.stride() != v_cache.stride() or k_cache.stride(-1) != 1 or k_cache.shape[0] != num_kv_heads:
+        raise RuntimeError("k_cache/v_cache must be [Hkv, capacity, 128] views with equal strides")
+    es = k_cache.element_size()
+    _lib.check(_lib.load().rt_qk_norm_rope_append(
+        qkv.data_ptr(), n, num_q_heads, num_kv_heads, 128, _ptr(q_norm_w), _ptr(k_norm_w), float(eps),
+        cos_table.data_ptr(), sin_table.data_ptr(), cos_table.shape[0], positions.data_ptr(), q_out.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), k_cache.stride(0) * es, k_cache.stride(1) * es, k_cache.shape[1],
+        int(offset), _ptr(offset_dev), status_tensor(qkv.device).data_ptr(), _stream(qkv.device)),
+        "rt_qk_norm_rope_append")
+    _count()
+    return q_out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """``out = silu(gate) * up`` over ``gate_up = [gate | up]`` rows (bf16)."""
+    _require_cuda(gate_up, out)
+    _rows_bf16(gate_up, "gate_up")
+    _rows_bf16(out, "out")
+    inter = out.shape[-1]
+    rows = out.numel() // inter
+    if gate_up.numel() != 2 * rows * inter:
+        raise RuntimeError("gate_up must hold [rows, 2 * inter]")
+    _lib.check(_lib.load().rt_silu_mul(gate_up.data_ptr(), out.data_ptr(), rows, inter, _stream(out.device)),
+               "rt_silu_mul")
+    _count()
+    return out

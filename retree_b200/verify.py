@@ -28,6 +28,7 @@ from types import SimpleNamespace
 
 import torch
 
+from . import fused as fused_mod
 from . import kernels
 from .attention import NAME as ATTN_NAME
 from .headsplit import NAME as HEADSPLIT_NAME
@@ -56,7 +57,7 @@ def extract_context_feature(hidden_states, layer_ids):
 
 class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
-                 temperature: float = 0.0, target_layer_ids=None, device=None):
+                 temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -101,6 +102,13 @@ class TreeVerifier:
         self.timed = False
         self.debug = False  # keep the posterior and the pre-compaction cache of the last round
         self.strategy, self.params = resolve_strategy()
+        # verify forward: fused stages (retree_b200.fused) unless the model is not
+        # one they cover or the caller needs the HF hidden states
+        if fused is None:
+            fused = target_layer_ids is None and fused_mod.supports(target)
+        if fused and target_layer_ids is not None:
+            raise RuntimeError("the fused verify forward does not return hidden states")
+        self.fused = fused_mod.FusedTarget(target, self.cache, self.n_max) if fused else None
 
     # ------------------------------------------------------------------ prefill
     @torch.inference_mode()
@@ -175,9 +183,13 @@ class TreeVerifier:
         ids = self.tree["verify_ids"][:n].view(1, n)
         pos = self.tree["verify_pos"][:n].view(1, n)
         bits = self.tree["mask"][:n]
-        mask = attach(bits.view(1, 1, n, self.words), bits, prefix_dev=self.start_dev[:1])
-        out = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache, use_cache=True)
-        posterior = sample(out.logits, self.temperature)
+        if self.fused is not None:
+            logits = self.fused.forward(ids[0], pos[0], bits, offset_dev=self.start_dev[:1]).unsqueeze(0)
+        else:
+            mask = attach(bits.view(1, 1, n, self.words), bits, prefix_dev=self.start_dev[:1])
+            logits = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache,
+                                 use_cache=True).logits
+        posterior = sample(logits, self.temperature)
         kernels.tree_walk(self.tree["parents"], self.tree["tokens"], posterior[0], count=count, out=self.walk,
                           verify_ids=self.tree["verify_ids"], output_ids=self.output_ids, start_dev=self.start_dev)
         kernels.kv_compact(self.cache.slab, 0, self.walk["accepted"], cur_length=n,
@@ -247,8 +259,11 @@ class TreeVerifier:
         mask = attach(bits.view(1, 1, n, self.words), bits)
         t = self._tick("tree_compile", t)
         # 2. verify forward
-        out = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache, use_cache=True,
-                          output_hidden_states=self.target_layer_ids is not None)
+        if self.fused is not None:
+            out = SimpleNamespace(logits=self.fused.forward(ids[0], pos[0], bits, offset=start).unsqueeze(0))
+        else:
+            out = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache,
+                              use_cache=True, output_hidden_states=self.target_layer_ids is not None)
         t = self._tick("verify", t)
         # 3.-5. posterior, walk, commit, compaction
         posterior = sample(out.logits, self.temperature)
