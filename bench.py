@@ -64,6 +64,8 @@ def parse():
     ap.add_argument("--cpu-sample-rounds", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from Python instead of graph replays")
+    ap.add_argument("--gemm", choices=("auto", "tcgen05", "cublas"), default="auto",
+                    help="projections of the fused verify forward")
     ap.add_argument("--hf-forward", action="store_true",
                     help="run the verify forward through the transformers modules instead of the fused stages")
     return ap.parse_args()
@@ -221,7 +223,7 @@ def run_ours(args, wl, rank, world, local_rank):
 
     def fresh():
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
-                         fused=not args.hf_forward)
+                         fused=not args.hf_forward, gemm=args.gemm)
         if wl.get("split"):
             v.prefill_random(wl["prompt"], seed=req)
         else:
@@ -282,6 +284,8 @@ def run_ours(args, wl, rank, world, local_rank):
     dev_s = float(dev_ms.item()) / 1000.0
 
     log(rank, "timed rounds done")
+    projections = None if v.fused is None else {
+        kd: ("rt_linear" if use else "cublas") for kd, use in v.fused.use_rt.items()}
     # ---- the tree-attention kernel on the live cache: all layers back to back, as in the round ----
     n_tree = 1 + wl["budget"]
     L_live = v.start
@@ -377,7 +381,8 @@ def run_ours(args, wl, rank, world, local_rank):
                                                       "weights)",
         "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": wl["prompt"],
                    "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
-                   "verify_forward": "transformers modules" if args.hf_forward else "fused stages",
+                   "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
+                   "projections": projections,
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer)"
                                    if wl.get("split") else f"dp{world} (one request per GPU)" + (
                                        ", recovery-delta all-gather per step" if world > 1 else "")),

@@ -280,6 +280,58 @@ int rt_qk_norm_rope_append(const void* qkv, int n, int num_q_heads, int num_kv_h
                            rt_stream_t stream);
 int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, rt_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Projections of the verify forward on tcgen05 (bf16 in, fp32 accumulate):
+ * Y[m, n_out] = X[m, k] . W[n_out, k]^T for m <= 512 tree nodes, with W
+ * row-major contiguous (the nn.Linear weights of Qwen3Attention / Qwen3MLP,
+ * models/qwen3/modeling_qwen3.py:236-247 and :70-83, and the lm_head).
+ * X rows are ld_x elements apart.  n_out % 128 == 0, k % 8 == 0, X / W /
+ * out 16-byte aligned, ld_x and ld_out multiples of 8.
+ *
+ * epilogue:
+ *   RT_EPI_STORE     out[i, :n_out] = bf16(Y[i]) (row stride ld_out);
+ *   RT_EPI_SILU_MUL  W = [gate; up] (n_out = 2 * inter): out[i, :inter] =
+ *                    bf16(bf16(silu(bf16(Y[i, :inter]))) * bf16(Y[i, inter:]))
+ *                    (Qwen3MLP.forward, modeling_qwen3.py:81-83);
+ *   RT_EPI_QKV_ROPE  W = [Wq; Wk; Wv] (n_out = (Hq + 2 Hkv) * 128): what
+ *                    rt_qk_norm_rope_append does with the bf16 result, with
+ *                    the arguments of *qkv (out / ld_out unused).
+ * When 128-row tiles alone do not cover the GPU, K is split over a cluster
+ * of up to 8 CTAs whose partial sums are added in a fixed order over
+ * distributed shared memory: no workspace, results independent of timing.
+ * rt_linear_check returns RT_OK when rt_linear takes the shape.
+ * ---------------------------------------------------------------------- */
+#define RT_EPI_STORE 0
+#define RT_EPI_SILU_MUL 1
+#define RT_EPI_QKV_ROPE 2
+
+typedef struct rt_qkv_epilogue {
+  int num_q_heads;
+  int num_kv_heads;
+  const void* q_norm_weight; /* bf16[128] or NULL (no head norm; then k_norm_weight NULL too) */
+  const void* k_norm_weight;
+  float eps;
+  const void* cos_table; /* bf16[table_len, 128] */
+  const void* sin_table;
+  int64_t table_len;
+  const int64_t* positions; /* [m] */
+  void* q_out;              /* bf16[m, Hq, 128] */
+  void* k_cache;            /* + g*cache_head_stride + row*cache_row_stride bytes */
+  void* v_cache;
+  int64_t cache_head_stride;
+  int64_t cache_row_stride;
+  int64_t capacity;
+  int64_t offset;
+  const int64_t* offset_dev; /* DEVICE; added to offset when non-NULL */
+} rt_qkv_epilogue;
+
+int rt_linear_check(int m, int n_out, int k, int epilogue);
+/* The launch rt_linear makes for this shape on the current device: K splits
+ * (cluster size), ring stages and shared memory per CTA (diagnostics). */
+int rt_linear_plan(int m, int n_out, int k, int epilogue, int* splits, int* stages, int* smem_bytes);
+int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* w, int n_out, int epilogue, void* out,
+              int64_t ld_out, const rt_qkv_epilogue* qkv, int* status, rt_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -45,7 +45,24 @@ SIGNATURES = {
     "rt_qk_norm_rope_append": (_I, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64,
                                     _I64, _I64, _P, _P, _P]),
     "rt_silu_mul": (_I, [_P, _P, _I, _I, _P]),
+    "rt_linear_check": (_I, [_I, _I, _I, _I]),
+    "rt_linear_plan": (_I, [_I, _I, _I, _I, _P, _P, _P]),
+    "rt_linear": (_I, [_P, _I64, _I, _I, _P, _I, _I, _P, _I64, _P, _P, _P]),
 }
+
+RT_EPI_STORE = 0
+RT_EPI_SILU_MUL = 1
+RT_EPI_QKV_ROPE = 2
+
+
+class QkvEpilogue(ctypes.Structure):
+    """``rt_qkv_epilogue`` (include/retree_b200.h), field for field."""
+
+    _fields_ = [("num_q_heads", ctypes.c_int), ("num_kv_heads", ctypes.c_int), ("q_norm_weight", _P),
+                ("k_norm_weight", _P), ("eps", ctypes.c_float), ("cos_table", _P), ("sin_table", _P),
+                ("table_len", ctypes.c_int64), ("positions", _P), ("q_out", _P), ("k_cache", _P), ("v_cache", _P),
+                ("cache_head_stride", ctypes.c_int64), ("cache_row_stride", ctypes.c_int64),
+                ("capacity", ctypes.c_int64), ("offset", ctypes.c_int64), ("offset_dev", _P)]
 
 # Host return codes / device status codes (include/retree_b200.h)
 RT_OK = 0

@@ -3,6 +3,7 @@
     python -m retree_b200.bench_kernels sweep  [--prefix 4096] [--budgets 16,32,64,128,256] [--layers 36]
     python -m retree_b200.bench_kernels single --budget 16 --prefix 2048 [--reps 3]
     python -m retree_b200.bench_kernels parts
+    python -m retree_b200.bench_kernels linear [--m 17,65,257] [--shapes qkv,o,gate_up,down,lm_head]
 
 ``sweep`` is the tree-verify attention budget sweep (Qwen3-4B head geometry:
 32 query / 8 KV heads, head_dim 128, bf16): random trees from seeded parent
@@ -12,7 +13,9 @@ layers captured in one CUDA graph and timed with CUDA events.  Each line
 reports the algorithmic bytes and FLOPs per launch, the achieved GB/s and
 TFLOP/s, and both as fractions of the measured peaks (MEASURED_PEAKS.json).
 ``single`` runs a few launches of one shape (for ncu captures); ``parts``
-times the draft top-k, the tree build and the compaction kernels.
+times the draft top-k, the tree build and the compaction kernels; ``linear``
+times rt_linear against cuBLAS on the Qwen3-4B projection shapes (36 weight
+copies per graph, so every launch streams its weights from HBM).
 """
 
 from __future__ import annotations
@@ -126,9 +129,49 @@ def parts(dev) -> list[dict]:
     return out
 
 
+LINEAR_SHAPES = {  # Qwen3-4B projections (n_out, k, epilogue)
+    "qkv": (6144, 2560, 0), "o": (2560, 4096, 0), "gate_up": (19456, 2560, 1), "down": (2560, 9728, 0),
+    "lm_head": (151936, 2560, 0)}
+
+
+def linear_case(name: str, m: int, layers: int, dev) -> list[dict]:
+    """rt_linear vs cuBLAS (torch.mm) on one projection shape, ``layers`` weight copies per graph."""
+    n_out, k, epi = LINEAR_SHAPES[name]
+    copies = 1 if name == "lm_head" else layers
+    g = torch.Generator(device=dev).manual_seed(0)
+    ws = [(torch.randn((n_out, k), device=dev, generator=g) * 0.02).to(torch.bfloat16) for _ in range(copies)]
+    x = torch.randn((m, k), device=dev, generator=g).to(torch.bfloat16)
+    width = n_out // 2 if epi == 1 else n_out
+    out = torch.empty((m, width), dtype=torch.bfloat16, device=dev)
+    full = torch.empty((m, n_out), dtype=torch.bfloat16, device=dev)
+    hbm, tf, kind = peaks()
+    rows = []
+    for impl in ("rt_linear", "cublas"):
+        def run():
+            for w in ws:
+                if impl == "rt_linear":
+                    kernels.linear(x, w, out=out, epilogue=epi)
+                elif epi == 1:
+                    torch.mm(x, w.t(), out=full)
+                    kernels.silu_mul(full, out)
+                else:
+                    torch.mm(x, w.t(), out=out)
+        us = graph_time_us(run, reps=10) / copies
+        kernels.check_device_status(dev)
+        b = n_out * k * 2 + m * k * 2 + m * width * 2
+        rows.append(dict(kernel="linear", shape=name, impl=impl, m=m, n_out=n_out, k=k, us=us, bytes=b,
+                         gbs=b / us / 1e3, hbm_frac=b / us / 1e3 / hbm, peak_kind=kind,
+                         plan=kernels.linear_plan(m, n_out, k, epi) if impl == "rt_linear" else None))
+    del ws
+    torch.cuda.empty_cache()
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("mode", choices=("sweep", "single", "parts"))
+    ap.add_argument("mode", choices=("sweep", "single", "parts", "linear"))
+    ap.add_argument("--m", default="17,65,257")
+    ap.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
     ap.add_argument("--prefix", type=int, default=4096)
     ap.add_argument("--budgets", default="16,32,64,128,256")
     ap.add_argument("--budget", type=int, default=16)
@@ -151,6 +194,11 @@ def main():
         torch.cuda.synchronize()
         kernels.check_device_status(dev)
         print(json.dumps(dict(ok=True, budget=a.budget, prefix=a.prefix)))
+    elif a.mode == "linear":
+        for m in (int(x) for x in a.m.split(",")):
+            for name in a.shapes.split(","):
+                for row in linear_case(name, m, a.layers, dev):
+                    print(json.dumps(row), flush=True)
     else:
         for row in parts(dev):
             print(json.dumps(row), flush=True)

@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <utility>
 
 #include "../../include/retree_b200.h"
 #include <cstdint>
@@ -38,5 +39,40 @@ inline void set_smem_limit(Kernel k, size_t bytes) {
 }
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Whether launches of the verify-forward kernels carry the programmatic
+// stream-serialisation attribute (RETREE_B200_PDL=0 turns it off).
+bool pdl_enabled();
+
+// cudaLaunchKernelEx with programmatic dependent launch (when enabled) and an
+// optional (1, cluster_y, 1) thread-block cluster.  Every kernel launched
+// through here calls pdl_wait() before it reads or writes data that earlier
+// kernels of the stream produce or consume.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_ex(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             int cluster_y, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  unsigned n = 0;
+  if (pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 1) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = 1;
+    attrs[n].val.clusterDim.y = static_cast<unsigned>(cluster_y);
+    attrs[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace rt

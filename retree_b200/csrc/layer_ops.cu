@@ -27,31 +27,10 @@
 
 #include "common.cuh"
 #include "host_util.h"
+#include "layer_math.cuh"
 
 namespace rt {
 namespace {
-
-__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
-struct alignas(16) Vec8 {
-  __nv_bfloat162 h[4];
-};
-
-__device__ __forceinline__ void unpack8(const Vec8& v, float* f) {
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 p = __bfloat1622float2(v.h[i]);
-    f[2 * i] = p.x;
-    f[2 * i + 1] = p.y;
-  }
-}
-
-__device__ __forceinline__ Vec8 pack8(const float* f) {
-  Vec8 v;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) v.h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
-  return v;
-}
 
 constexpr int kNormThreads = 128;
 constexpr int kNormMaxVec = 16;  // hidden <= 128 threads * 16 vectors * 8 = 16384
@@ -68,10 +47,13 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return s;
 }
 
-// One CTA per token row.  mode 0: residual = embed[ids[row]];  mode 1:
-// residual = bf16(residual + delta);  mode 2: the row is `residual` as is.
-// out = bf16(weight * bf16(x * rsqrt(mean(x^2) + eps)))  (Qwen3RMSNorm.forward,
-// modeling_qwen3.py:59-64, and the residual adds at :327 and :333).
+// One CTA per token row, V 16-byte vectors per thread.  mode 0: residual =
+// embed[ids[row]];  mode 1: residual = bf16(residual + delta);  mode 2: the
+// row is `residual` as is.  out = bf16(weight * bf16(x * rsqrt(mean(x^2) +
+// eps)))  (Qwen3RMSNorm.forward, modeling_qwen3.py:59-64, and the residual
+// adds at :327 and :333).  Every load of the row (input, delta, weight) is
+// issued before the first store, so a launch costs one memory round trip.
+template <int V>
 __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     int mode, const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ embed, int64_t vocab,
     const __nv_bfloat16* __restrict__ delta, __nv_bfloat16* __restrict__ residual,
@@ -80,6 +62,16 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   __shared__ float red[kNormThreads / 32];
   const int row = blockIdx.x;
   const int nvec = hidden >> 3;
+  pdl_launch_dependents();
+  // the norm weights are not written by the round: fetch them before waiting
+  const Vec8* wv = reinterpret_cast<const Vec8*>(weight);
+  Vec8 wr[V];
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int v = threadIdx.x + j * kNormThreads;
+    if (v < nvec) wr[j] = wv[v];
+  }
+  pdl_wait();
   const Vec8* src;
   bool zero = false;
   if (mode == 0) {
@@ -93,21 +85,30 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
     src = reinterpret_cast<const Vec8*>(residual + static_cast<int64_t>(row) * hidden);
   }
   const Vec8* dsrc = reinterpret_cast<const Vec8*>(delta + static_cast<int64_t>(row) * hidden);
-  Vec8* rdst = reinterpret_cast<Vec8*>(residual + static_cast<int64_t>(row) * hidden);
-  float x[kNormMaxVec][8];
-  float ss = 0.f;
+  Vec8 xr[V], dr[V];
 #pragma unroll
-  for (int j = 0; j < kNormMaxVec; ++j) {
+  for (int j = 0; j < V; ++j) {
     const int v = threadIdx.x + j * kNormThreads;
     if (v < nvec) {
-      unpack8(src[v], x[j]);
+      xr[j] = src[v];
+      if (mode == 1) dr[j] = dsrc[v];
+    }
+  }
+  Vec8* rdst = reinterpret_cast<Vec8*>(residual + static_cast<int64_t>(row) * hidden);
+  float x[V][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < V; ++j) {
+    const int v = threadIdx.x + j * kNormThreads;
+    if (v < nvec) {
+      unpack8(xr[j], x[j]);
       if (zero) {
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[j][e] = 0.f;
       }
       if (mode == 1) {
         float d[8];
-        unpack8(dsrc[v], d);
+        unpack8(dr[j], d);
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[j][e] = round_bf16(x[j][e] + d[e]);
       }
@@ -118,19 +119,39 @@ __global__ void __launch_bounds__(kNormThreads) add_rmsnorm_kernel(
   }
   const float var = block_sum(ss, red) * (1.0f / static_cast<float>(hidden));
   const float r = rsqrtf(var + eps);
-  const Vec8* wv = reinterpret_cast<const Vec8*>(weight);
   Vec8* o = reinterpret_cast<Vec8*>(out + static_cast<int64_t>(row) * hidden);
 #pragma unroll
-  for (int j = 0; j < kNormMaxVec; ++j) {
+  for (int j = 0; j < V; ++j) {
     const int v = threadIdx.x + j * kNormThreads;
     if (v < nvec) {
       float w[8], y[8];
-      unpack8(wv[v], w);
+      unpack8(wr[j], w);
 #pragma unroll
       for (int e = 0; e < 8; ++e) y[e] = w[e] * round_bf16(x[j][e] * r);
       o[v] = pack8(y);
     }
   }
+}
+
+template <int V>
+void launch_norm(int mode, const int64_t* ids, const void* embed, int64_t vocab, const void* delta, void* residual,
+                 const void* weight, void* out, int rows, int hidden, float eps, int* status, cudaStream_t s) {
+  launch_ex(add_rmsnorm_kernel<V>, dim3(rows), dim3(kNormThreads), 0, s, 1, mode, ids,
+            static_cast<const __nv_bfloat16*>(embed), vocab, static_cast<const __nv_bfloat16*>(delta),
+            static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(weight),
+            static_cast<__nv_bfloat16*>(out), hidden, eps, status);
+}
+
+void dispatch_norm(int mode, const int64_t* ids, const void* embed, int64_t vocab, const void* delta,
+                   void* residual, const void* weight, void* out, int rows, int hidden, float eps, int* status,
+                   cudaStream_t s) {
+  const int per = (hidden / 8 + kNormThreads - 1) / kNormThreads;
+  if (per <= 1) launch_norm<1>(mode, ids, embed, vocab, delta, residual, weight, out, rows, hidden, eps, status, s);
+  else if (per <= 2) launch_norm<2>(mode, ids, embed, vocab, delta, residual, weight, out, rows, hidden, eps, status, s);
+  else if (per <= 3) launch_norm<3>(mode, ids, embed, vocab, delta, residual, weight, out, rows, hidden, eps, status, s);
+  else if (per <= 4) launch_norm<4>(mode, ids, embed, vocab, delta, residual, weight, out, rows, hidden, eps, status, s);
+  else if (per <= 8) launch_norm<8>(mode, ids, embed, vocab, delta, residual, weight, out, rows, hidden, eps, status, s);
+  else launch_norm<kNormMaxVec>(mode, ids, embed, vocab, delta, residual, weight, out, rows, hidden, eps, status, s);
 }
 
 // One warp per (token, head slot); slots [0, hq) are query heads, [hq, hq+hkv)
@@ -147,6 +168,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_kernel(
     __nv_bfloat16* __restrict__ q_out, char* k_cache, char* v_cache, int64_t c_head_stride, int64_t c_row_stride,
     int64_t capacity, int64_t offset, const int64_t* offset_dev, int* status) {
   constexpr int D = 128;
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int slots = hq + 2 * hkv;
@@ -158,50 +181,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_kernel(
   uint2 res = raw;
   if (!is_v) {
     float x[4];
-    {
-      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-      x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
-    }
-    const __nv_bfloat16* nw = s < hq ? q_norm_w : k_norm_w;
-    if (nw != nullptr) {
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) ss = __fadd_rn(ss, __fmul_rn(x[e], x[e]));
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
-      const float r = rsqrtf(ss * (1.0f / D) + eps);
-      const uint2 wr = reinterpret_cast<const uint2*>(nw)[lane];
-      const float2 wa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wr.x));
-      const float2 wb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wr.y));
-      const float w[4] = {wa.x, wa.y, wb.x, wb.y};
-#pragma unroll
-      for (int e = 0; e < 4; ++e) x[e] = round_bf16(w[e] * round_bf16(x[e] * r));
-    }
+    unpack4(raw, x);
     int64_t p = positions[t];
     if (p < 0 || p >= table_len) {
       if (lane == 0) set_status(status, RT_DEV_BAD_INDEX);
       p = 0;
     }
-    const uint2 cr = reinterpret_cast<const uint2*>(cos_t + p * D)[lane];
-    const uint2 sr = reinterpret_cast<const uint2*>(sin_t + p * D)[lane];
-    const float2 ca = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&cr.x));
-    const float2 cb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&cr.y));
-    const float2 sa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sr.x));
-    const float2 sb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&sr.y));
-    const float c[4] = {ca.x, ca.y, cb.x, cb.y};
-    const float sn[4] = {sa.x, sa.y, sb.x, sb.y};
-    float y[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float other = __shfl_xor_sync(0xFFFFFFFFu, x[e], 16);
-      const float rot = lane < 16 ? -other : other;
-      y[e] = round_bf16(x[e] * c[e]) + round_bf16(rot * sn[e]);
-    }
-    const __nv_bfloat162 ya = __floats2bfloat162_rn(y[0], y[1]);
-    const __nv_bfloat162 yb = __floats2bfloat162_rn(y[2], y[3]);
-    res.x = *reinterpret_cast<const uint32_t*>(&ya);
-    res.y = *reinterpret_cast<const uint32_t*>(&yb);
+    res = qk_norm_rope4(x, s < hq ? q_norm_w : k_norm_w, eps, cos_t + p * D, sin_t + p * D, lane);
   }
   if (s < hq) {
     reinterpret_cast<uint2*>(q_out + (static_cast<int64_t>(t) * hq + s) * D)[lane] = res;
@@ -223,6 +209,8 @@ __global__ void __launch_bounds__(256) qk_norm_rope_append_kernel(
 // fp32 as torch's CUDA kernel evaluates it).
 __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __restrict__ gate_up,
                                                        __nv_bfloat16* __restrict__ out, int rows, int inter) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int vpr = inter >> 3;
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<int64_t>(rows) * vpr) return;
@@ -233,7 +221,7 @@ __global__ void __launch_bounds__(256) silu_mul_kernel(const __nv_bfloat16* __re
   unpack8(g[v], a);
   unpack8(g[vpr + v], b);
 #pragma unroll
-  for (int e = 0; e < 8; ++e) y[e] = round_bf16(a[e] / (1.0f + expf(-a[e]))) * b[e];
+  for (int e = 0; e < 8; ++e) y[e] = silu_mul_bf16(a[e], b[e]);
   reinterpret_cast<Vec8*>(out + r * inter)[v] = pack8(y);
 }
 
@@ -255,9 +243,8 @@ extern "C" int rt_embed_rmsnorm(const int64_t* ids, const void* table, int64_t v
       !aligned16(weight) || !aligned16(out)) {
     return RT_ERR_INVALID_ARGUMENT;
   }
-  add_rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      0, ids, static_cast<const __nv_bfloat16*>(table), vocab, nullptr, static_cast<__nv_bfloat16*>(residual),
-      static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out), hidden, eps, status);
+  dispatch_norm(0, ids, table, vocab, nullptr, residual, weight, out, rows, hidden, eps, status,
+                static_cast<cudaStream_t>(stream));
   return check_launch();
 }
 
@@ -271,10 +258,8 @@ extern "C" int rt_add_rmsnorm(const void* delta, void* residual, const void* wei
       (delta && !aligned16(delta))) {
     return RT_ERR_INVALID_ARGUMENT;
   }
-  add_rmsnorm_kernel<<<rows, kNormThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      delta ? 1 : 2, nullptr, nullptr, 0, static_cast<const __nv_bfloat16*>(delta),
-      static_cast<__nv_bfloat16*>(residual), static_cast<const __nv_bfloat16*>(weight),
-      static_cast<__nv_bfloat16*>(out), hidden, eps, nullptr);
+  dispatch_norm(delta ? 1 : 2, nullptr, nullptr, 0, delta, residual, weight, out, rows, hidden, eps, nullptr,
+                static_cast<cudaStream_t>(stream));
   return check_launch();
 }
 
@@ -303,7 +288,7 @@ extern "C" int rt_qk_norm_rope_append(const void* qkv, int n, int num_q_heads, i
   }
   const int64_t warps = static_cast<int64_t>(n) * (num_q_heads + 2 * num_kv_heads);
   const int blocks = static_cast<int>((warps * 32 + 255) / 256);
-  qk_norm_rope_append_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  launch_ex(qk_norm_rope_append_kernel, dim3(blocks), dim3(256), 0, static_cast<cudaStream_t>(stream), 1,
       static_cast<const __nv_bfloat16*>(qkv), n, num_q_heads, num_kv_heads,
       static_cast<const __nv_bfloat16*>(q_norm_weight), static_cast<const __nv_bfloat16*>(k_norm_weight), eps,
       static_cast<const __nv_bfloat16*>(cos_table), static_cast<const __nv_bfloat16*>(sin_table), table_len,
@@ -317,7 +302,8 @@ extern "C" int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, 
   if (rows == 0) return RT_OK;
   if (!gate_up || !out || !aligned16(gate_up) || !aligned16(out)) return RT_ERR_INVALID_ARGUMENT;
   const int64_t total = static_cast<int64_t>(rows) * (inter / 8);
-  silu_mul_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), rows, inter);
+  launch_ex(silu_mul_kernel, dim3(static_cast<unsigned>((total + 255) / 256)), dim3(256), 0,
+            static_cast<cudaStream_t>(stream), 1, static_cast<const __nv_bfloat16*>(gate_up),
+            static_cast<__nv_bfloat16*>(out), rows, inter);
   return check_launch();
 }

@@ -2,8 +2,19 @@
 #include "common.cuh"
 #include "host_util.h"
 
+#include <cstdlib>
+#include <cstring>
+
 namespace rt {
 thread_local int g_last_cuda_error = 0;
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("RETREE_B200_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
 }
 
 extern "C" int rt_abi_version(void) { return 2; }

@@ -1,0 +1,61 @@
+// Host-side tensor-map (TMA descriptor) encoding, through the driver entry
+// point fetched by the runtime (no link-time dependency on libcuda).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdlib>
+
+#include "../../include/retree_b200.h"
+
+namespace rt {
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+inline EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<EncodeTiledFn>(ptr);
+    return static_cast<EncodeTiledFn>(nullptr);
+  }();
+  return fn;
+}
+
+// Row-major bf16 matrix [rows][cols] (row stride `ld` elements) read in boxes
+// of box_rows x 64 columns with the 128-byte swizzle; out-of-range rows and
+// columns read as zero.
+inline CUtensorMapL2promotion l2_promotion() {
+  static const CUtensorMapL2promotion v = [] {
+    const char* e = std::getenv("RETREE_B200_L2PROMO");
+    switch (e ? std::atoi(e) : 3) {
+      case 0: return CU_TENSOR_MAP_L2_PROMOTION_NONE;
+      case 1: return CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
+      case 2: return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+      default: return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+    }
+  }();
+  return v;
+}
+
+inline int make_bf16_2d_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld,
+                             uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return RT_ERR_CUDA;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  const cuuint32_t box[2] = {64, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, l2_promotion(),
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? RT_OK : RT_ERR_INVALID_ARGUMENT;
+}
+
+}  // namespace rt

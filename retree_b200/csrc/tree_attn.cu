@@ -31,6 +31,7 @@
 
 #include "common.cuh"
 #include "host_util.h"
+#include "tmap.h"
 
 namespace rt {
 
@@ -149,6 +150,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   Barriers& bar = *reinterpret_cast<Barriers*>(smem + kOffBar);
+  // Programmatic dependent launch: the prefix rows of the KV cache are not
+  // written while the round's forward runs (only rows from prefix_len on, by
+  // this layer's projection), so the producer requests the leading pure-prefix
+  // K/V blocks before waiting for the previous kernel; Q, the tree block, the
+  // mask and every write come after the wait.
+  pdl_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, mt = blockIdx.z;
   const int G = p.group;
@@ -161,9 +168,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   split_range(total_keys, split, p.num_splits, kBN, b0, b1);
   const int nb = static_cast<int>(b1 - b0);
   if (nb <= 0) {
+    pdl_wait();
     if (p.num_splits > 1) write_neutral_partial(p, split, kvh, row0, min(kBM, rows_total - row0));
     return;
   }
+  // leading blocks of this split that hold prefix keys only (at most the ring depth)
+  int pre = 0;
+  while (pre < min(2, nb) && (b0 + pre + 1) * kBN <= L) ++pre;
 
   if (tid == 0) {
     mbar_init(&bar.full_q, 1);
@@ -186,6 +197,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tmem_relinquish();
   }
   if (!q_tma) {
+    pdl_wait();
     // Q tile -> SW128 K-major smem by plain loads (group sizes that do not tile 128 rows)
     constexpr int kPer = (kBM * 16 + kAttnThreads - 1) / kAttnThreads;
     uint4 v[kPer];
@@ -219,17 +231,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (warp == kProducerWarp) {
     // ---------------- TMA producer: lane 0 Q and K, lane 1 V ----------------
     if (lane == 0) {
-      if (q_tma) {
-        prefetch_tmap(&tmap_q);
-        mbar_arrive_expect_tx(&bar.full_q, kTile);
-        const int tok0 = mt * (kBM / G);
-        tma_load_3d(smem + kOffQ, &tmap_q, &bar.full_q, 0, kvh * G, tok0);
-        tma_load_3d(smem + kOffQ + kHalf, &tmap_q, &bar.full_q, 64, kvh * G, tok0);
-      } else {
-        mbar_arrive(&bar.full_q);
-      }
+      auto issue_q = [&] {
+        pdl_wait();
+        if (q_tma) {
+          mbar_arrive_expect_tx(&bar.full_q, kTile);
+          const int tok0 = mt * (kBM / G);
+          tma_load_3d(smem + kOffQ, &tmap_q, &bar.full_q, 0, kvh * G, tok0);
+          tma_load_3d(smem + kOffQ + kHalf, &tmap_q, &bar.full_q, 64, kvh * G, tok0);
+        } else {
+          mbar_arrive(&bar.full_q);
+        }
+      };
+      if (q_tma) prefetch_tmap(&tmap_q);
       int issued = 0;
+      bool q_issued = false;
       for (int j = 0; j < nb; ++j) {
+        if (j == pre) {
+          issue_q();
+          q_issued = true;
+        }
         const int st = j & 1;
         // stage st is free once S(j-2) has consumed it
         if (!mbar_wait(&bar.empty_k[st], ((j >> 1) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
@@ -240,6 +260,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tma_load_3d(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh);
         issued = j + 1;
       }
+      if (!q_issued) issue_q();
       if (*abort_flag) {
         mbar_wait(&bar.full_q, 0, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
         for (int j = max(0, issued - 2); j < issued; ++j)
@@ -248,6 +269,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     } else if (lane == 1) {
       int issued = 0;
       for (int j = 0; j < nb; ++j) {
+        if (j == pre) pdl_wait();
         const int st = j & 1;
         // stage st is free once PV(j-2) has consumed it
         if (!mbar_wait(&bar.empty_v[st], ((j >> 1) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
@@ -261,8 +283,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (*abort_flag)
         for (int j = max(0, issued - 2); j < issued; ++j)
           mbar_wait(&bar.full_v[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+      pdl_wait();
+    } else {
+      pdl_wait();
     }
   } else if (warp == kMmaWarp) {
+    pdl_wait();
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(kBM, kBN, false, false);
@@ -314,6 +340,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else {
     // ---------------- softmax / epilogue (warps 0-7) ----------------
+    pdl_wait();
     // Warp w reads TMEM lanes 32*(w%4)..+31 (its sub-partition) and owns key /
     // head-dim columns [64*half, 64*half + 64) with half = w / 4, so every tile
     // row is handled by two threads that exchange their partial max and sum.
@@ -497,6 +524,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 constexpr int kSimtKeys = 64;
 
 __global__ void __launch_bounds__(128) tree_attn_simt_kernel(const AttnParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ __align__(16) __nv_bfloat16 ks[kSimtKeys][kHD];
   __shared__ __align__(16) __nv_bfloat16 vs[kSimtKeys][kHD];
   const int split = blockIdx.x, kvh = blockIdx.y;
@@ -617,30 +646,52 @@ __global__ void __launch_bounds__(128) tree_attn_simt_kernel(const AttnParams p)
 // Split merge: one warp per (kv head, tile row); lane owns 4 dims.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int rows = p.n * p.group;
   if (gw >= p.num_kv_heads * rows) return;
   const int kvh = gw / rows, R = gw - kvh * rows;
   const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
-  float M = -INFINITY;
-  for (int s = 0; s < p.num_splits; ++s)
-    M = fmaxf(M, p.ws_ml[(static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R].x);
+  const int S = p.num_splits;
+  auto slot = [&](int s) { return (static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R; };
+  // lane s holds split s's (max, sum); one load per lane instead of a serial walk
+  const float2 none = make_float2(-INFINITY, 0.f);
+  const float2 first = lane < S ? p.ws_ml[slot(lane)] : none;
+  float M = first.x;
+  for (int base = 32; base < S; base += 32) M = fmaxf(M, base + lane < S ? p.ws_ml[slot(base + lane)].x : -INFINITY);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, o));
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   float lsum = 0.f;
   if (M > -INFINITY) {
-    for (int s = 0; s < p.num_splits; ++s) {
-      const int64_t idx = (static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R;
-      const float2 ml = p.ws_ml[idx];
-      if (ml.x == -INFINITY) continue;
-      const float w = ex2(ml.x - M);
-      const float4 o = *reinterpret_cast<const float4*>(p.ws_o + idx * kHD + lane * 4);
-      acc.x += w * o.x;
-      acc.y += w * o.y;
-      acc.z += w * o.z;
-      acc.w += w * o.w;
+    for (int base = 0; base < S; base += 32) {
+      const float2 ml = base == 0 ? first : (base + lane < S ? p.ws_ml[slot(base + lane)] : none);
+      const float w = ml.x == -INFINITY ? 0.f : ex2(ml.x - M);
       lsum += w * ml.y;
+      const int cnt = min(32, S - base);
+      for (int j = 0; j < cnt; j += 8) {
+        float4 o[8];
+        float ww[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          ww[u] = __shfl_sync(0xFFFFFFFFu, w, (j + u) & 31);
+          o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (j + u < cnt && ww[u] != 0.f)
+            o[u] = *reinterpret_cast<const float4*>(p.ws_o + slot(base + j + u) * kHD + lane * 4);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          acc.x = fmaf(ww[u], o[u].x, acc.x);
+          acc.y = fmaf(ww[u], o[u].y, acc.y);
+          acc.z = fmaf(ww[u], o[u].z, acc.z);
+          acc.w = fmaf(ww[u], o[u].w, acc.w);
+        }
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, o);
   }
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
   const int node = R / p.group, h = kvh * p.group + (R - node * p.group);
@@ -653,24 +704,6 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static bool tried = false;
-  if (!tried) {
-    tried = true;
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  }
-  return fn;
-}
-
 static int make_kv_tmap(CUtensorMap* m, const void* base, int64_t head_stride, int64_t row_stride, int64_t capacity,
                         int heads) {
   EncodeTiledFn fn = encode_fn();
@@ -808,16 +841,16 @@ extern "C" int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_
     }
     set_smem_limit(tree_attn_tc_kernel, kAttnSmem);
     const dim3 grid(num_splits, num_kv_heads, p.tiles);
-    tree_attn_tc_kernel<<<grid, kAttnThreads, kAttnSmem, s>>>(tk, tv, tq, p, q_tma);
+    rc = record_cuda(launch_ex(tree_attn_tc_kernel, grid, dim3(kAttnThreads), kAttnSmem, s, 1, tk, tv, tq, p, q_tma));
+    if (rc != RT_OK) return rc;
   } else {
     const dim3 grid(num_splits, num_kv_heads);
-    tree_attn_simt_kernel<<<grid, 128, 0, s>>>(p);
+    int rc = record_cuda(launch_ex(tree_attn_simt_kernel, grid, dim3(128), 0, s, 1, p));
+    if (rc != RT_OK) return rc;
   }
-  int rc = check_launch();
-  if (rc != RT_OK || num_splits == 1) return rc;
+  if (num_splits == 1) return RT_OK;
   const int warps = num_kv_heads * n * G;
-  attn_combine_kernel<<<(warps + 3) / 4, 128, 0, s>>>(p);
-  return check_launch();
+  return record_cuda(launch_ex(attn_combine_kernel, dim3((warps + 3) / 4), dim3(128), 0, s, 1, p));
 }
 
 // ---------------------------------------------------------------------------

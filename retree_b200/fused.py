@@ -7,29 +7,33 @@ the module tree.  Per layer the HF forward (models/qwen3/modeling_qwen3.py:
 305-334 with Qwen3Attention.forward :252-299 and Qwen3MLP.forward :81-83)
 issues about forty kernels -- casts, the four RMSNorm steps, rotary slicing
 and concatenation, residual adds, the cache ``torch.cat`` -- around seven
-projections.  Here a layer is nine launches:
+projections.  Here a layer is seven launches:
 
-  rt_add_rmsnorm          residual += mlp_out; x = rmsnorm(residual) * w_in
-  x @ [Wq;Wk;Wv]^T        one cuBLAS GEMM over the packed projection
-  rt_qk_norm_rope_append  q/k head norms + rotary; q out, k/v into the cache
-  rt_tree_attn            the tree-masked attention kernel
-  attn @ Wo^T             cuBLAS
-  rt_add_rmsnorm          residual += o; x = rmsnorm(residual) * w_post
-  x @ [Wg;Wu]^T           one cuBLAS GEMM over the packed gate/up projection
-  rt_silu_mul             act = silu(gate) * up
-  act @ Wd^T              cuBLAS
+  rt_add_rmsnorm     residual += mlp_out; x = rmsnorm(residual) * w_in
+  rt_linear QKV      x @ [Wq;Wk;Wv]^T, epilogue: q/k head norms + rotary,
+                     q out, k/v into the cache
+  rt_tree_attn       the tree-masked attention kernel (+ split combine)
+  rt_linear          attn @ Wo^T
+  rt_add_rmsnorm     residual += o; x = rmsnorm(residual) * w_post
+  rt_linear SILU     x @ [Wg;Wu]^T, epilogue: silu(gate) * up
+  rt_linear          act @ Wd^T
 
 and the stack opens with ``rt_embed_rmsnorm`` (embedding lookup + first norm)
-and closes with the final norm and the lm_head GEMM.  The packed projection
-weights are single tensors whose row blocks the HF modules keep as views, so
-the model's memory does not grow and the HF forward stays usable (prefill
-runs through it).
+and closes with the final norm and the lm_head projection.  The projections
+are the tcgen05 kernel of ``csrc/linear.cu`` (``gemm="tcgen05"``) or cuBLAS
+followed by the standalone stage kernels (``gemm="cublas"``; also used for
+shapes ``rt_linear`` does not take and for biased projections); the default
+``gemm="auto"`` times both per projection kind on the model's own weights at
+construction and keeps the faster.
+The packed projection weights are single tensors whose row blocks the HF
+modules keep as views, so the model's memory does not grow and the HF
+forward stays usable (prefill runs through it).
 
 The rotary tables are the model's own ``rotary_emb`` outputs for positions
 ``[0, max_positions)`` (bf16, what HF computes per forward), so positions are
 device-side indices.  Numerics follow the HF ops' bf16 rounding points (see
-``csrc/layer_ops.cu``); the projections are the same cuBLAS GEMMs, run over
-the packed weights.
+``csrc/layer_ops.cu``); the projections accumulate in fp32 and round to bf16
+like the library GEMM, in their own summation order.
 """
 
 from __future__ import annotations
@@ -40,6 +44,8 @@ from torch import nn
 from . import kernels
 
 SUPPORTED_MODEL_TYPES = ("qwen3", "qwen2", "llama")
+
+_AUTOTUNE: dict = {}
 
 
 def supports(model) -> bool:
@@ -85,7 +91,7 @@ class _Layer:
 
 
 class FusedTarget:
-    def __init__(self, model, cache, n_max: int, max_positions: int | None = None):
+    def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto"):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -144,6 +150,18 @@ class FusedTarget:
         self.act = torch.empty((n, self.inter), **e)
         self.mlp_out = torch.empty((n, self.hidden), **e)
         self.logits = torch.empty((n, self.vocab), **e)
+        if gemm not in ("auto", "tcgen05", "cublas"):
+            raise ValueError("gemm must be 'auto', 'tcgen05' or 'cublas'")
+        self.gemm = gemm
+        # projection kind -> use rt_linear (True) or cuBLAS (False)
+        kinds = ("qkv", "o", "gate_up", "down", "lm_head")
+        self.use_rt = {kd: gemm == "tcgen05" for kd in kinds}
+        if gemm == "auto":
+            # one decision per process and shape, so every verifier of a model computes alike
+            key = (dev.index, self.n_max, self.hidden, self.inter, hq, hkv, self.vocab, len(self.layers))
+            if key not in _AUTOTUNE:
+                _AUTOTUNE[key] = self._autotune(self.n_max)
+            self.use_rt = dict(_AUTOTUNE[key])
 
     @staticmethod
     def _rope_tables(model, max_positions: int):
@@ -163,10 +181,93 @@ class FusedTarget:
     def _splits(self, n: int) -> int:
         return kernels.default_splits(n, self.hq, self.hkv, self.cache.capacity - n)
 
-    def _linear(self, x, w, b, out):
+    @torch.inference_mode()
+    def _autotune(self, n: int) -> dict:
+        """Per projection kind, whether rt_linear beats cuBLAS (+ the stage kernel) at n rows.
+
+        Each candidate runs over every layer's weights back to back (so the
+        weights stream from HBM as in a round), K/V going to scratch rows.
+        """
+        dev = self.device
+        x = torch.randn((n, max(self.hidden, self.inter, self.hq * self.head_dim)), device=dev).to(torch.bfloat16)
+        pos = torch.zeros(n, dtype=torch.int64, device=dev)
+        kv = torch.zeros((2, self.hkv, n, self.head_dim), dtype=torch.bfloat16, device=dev)
+        choice = {}
+
+        def timed(fn):
+            fn()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(3):
+                fn()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            return e0.elapsed_time(e1)
+
+        specs = {
+            "qkv": ([L.qkv_w for L in self.layers], self.hidden, 2, all(L.qkv_b is None for L in self.layers)),
+            "o": ([L.o_w for L in self.layers], self.hq * self.head_dim, 0, all(L.o_b is None for L in self.layers)),
+            "gate_up": ([L.gate_up_w for L in self.layers], self.hidden, 1, True),
+            "down": ([L.down_w for L in self.layers], self.inter, 0, True),
+            "lm_head": ([self.lm_head], self.hidden, 0, True),
+        }
+        for kind, (ws, k, epi, no_bias) in specs.items():
+            xk = x[:, :k]
+            if not no_bias or not kernels.linear_supported(n, ws[0].shape[0], k, epi):
+                choice[kind] = False
+                continue
+            L0 = self.layers[0]
+            qkv = dict(num_q_heads=self.hq, num_kv_heads=self.hkv, q_norm=L0.q_norm, k_norm=L0.k_norm,
+                       eps=L0.eps_qk, cos=self.cos, sin=self.sin, positions=pos, q_out=self.q[:n], k_cache=kv[0],
+                       v_cache=kv[1])
+            width = ws[0].shape[0] // 2 if epi == 1 else ws[0].shape[0]
+            out = self.logits[:n] if kind == "lm_head" else torch.empty((n, width), dtype=torch.bfloat16, device=dev)
+
+            def ours():
+                for w in ws:
+                    kernels.linear(xk, w, out=None if epi == 2 else out, epilogue=epi, qkv=qkv if epi == 2 else None)
+
+            def library():
+                for w in ws:
+                    if epi == 1:
+                        kernels.silu_mul(torch.mm(xk, w.t(), out=self.gate_up[:n]), out)
+                    elif epi == 2:
+                        y = torch.mm(xk, w.t(), out=self.qkv[:n])
+                        kernels.qk_norm_rope_append(y, self.hq, self.hkv, L0.q_norm, L0.k_norm, L0.eps_qk, self.cos,
+                                                    self.sin, pos, self.q[:n], kv[0], kv[1])
+                    else:
+                        torch.mm(xk, w.t(), out=out)
+
+            choice[kind] = timed(ours) < timed(library)
+        kernels.check_device_status(dev)
+        return choice
+
+    def _linear(self, x, w, b, out, epilogue: int = 0, kind: str = ""):
+        """One projection: rt_linear (tcgen05, fused epilogue) when chosen for this kind, else cuBLAS."""
+        m, k = x.shape
+        if self.use_rt.get(kind, False) and b is None and kernels.linear_supported(m, w.shape[0], k, epilogue):
+            return kernels.linear(x, w, out=out, epilogue=epilogue)
+        if epilogue == 1:
+            y = torch.mm(x, w.t(), out=self.gate_up[:m])
+            return kernels.silu_mul(y, out)
         if b is None:
             return torch.mm(x, w.t(), out=out)
         return torch.addmm(b, x, w.t(), out=out)
+
+    def _qkv(self, L, xn, positions, offset, offset_dev):
+        """Packed q/k/v projection + head norms + rotary + cache append."""
+        n = xn.shape[0]
+        kc, vc = self.cache.slab[2 * L.index], self.cache.slab[2 * L.index + 1]
+        if self.use_rt["qkv"] and L.qkv_b is None and kernels.linear_supported(n, L.qkv_w.shape[0], xn.shape[1], 2):
+            kernels.linear(xn, L.qkv_w, epilogue=2,
+                           qkv=dict(num_q_heads=L.hq, num_kv_heads=L.hkv, q_norm=L.q_norm, k_norm=L.k_norm,
+                                    eps=L.eps_qk, cos=self.cos, sin=self.sin, positions=positions, q_out=self.q[:n],
+                                    k_cache=kc, v_cache=vc, offset=offset, offset_dev=offset_dev))
+            return
+        self._linear(xn, L.qkv_w, L.qkv_b, self.qkv[:n], kind="qkv")
+        kernels.qk_norm_rope_append(self.qkv[:n], L.hq, L.hkv, L.q_norm, L.k_norm, L.eps_qk, self.cos, self.sin,
+                                    positions, self.q[:n], kc, vc, offset=offset, offset_dev=offset_dev)
 
     @torch.inference_mode()
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, bits: torch.Tensor, offset: int = 0,
@@ -192,10 +293,8 @@ class FusedTarget:
                 kernels.embed_rmsnorm(ids, self.embed, L.in_norm, L.eps_in, res, xn)
             else:
                 kernels.add_rmsnorm(self.mlp_out[:n], res, L.in_norm, L.eps_in, xn)
-            self._linear(xn, L.qkv_w, L.qkv_b, self.qkv[:n])
+            self._qkv(L, xn, positions, offset, offset_dev)
             kc, vc = slab[2 * L.index], slab[2 * L.index + 1]
-            kernels.qk_norm_rope_append(self.qkv[:n], L.hq, L.hkv, L.q_norm, L.k_norm, L.eps_qk, self.cos, self.sin,
-                                        positions, self.q[:n], kc, vc, offset=offset, offset_dev=offset_dev)
             if offset_dev is not None:
                 kernels.tree_attention(self.q[:n], kc, vc, bits, cap - n, scale=L.scale, out=self.attn[:n],
                                        num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap)
@@ -207,10 +306,9 @@ class FusedTarget:
                 from .headsplit import gather_heads
                 group, world, _ = L.split
                 attn = gather_heads(attn.unsqueeze(0), group, world)[0]
-            self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n])
+            self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n], kind="o")
             kernels.add_rmsnorm(self.o[:n], res, L.post_norm, L.eps_post, xn)
-            torch.mm(xn, L.gate_up_w.t(), out=self.gate_up[:n])
-            kernels.silu_mul(self.gate_up[:n], self.act[:n])
-            torch.mm(self.act[:n], L.down_w.t(), out=self.mlp_out[:n])
+            self._linear(xn, L.gate_up_w, None, self.act[:n], epilogue=1, kind="gate_up")
+            self._linear(self.act[:n], L.down_w, None, self.mlp_out[:n], kind="down")
         kernels.add_rmsnorm(self.mlp_out[:n], res, self.final_norm, self.eps, xn)
-        return torch.mm(xn, self.lm_head.t(), out=self.logits[:n])
+        return self._linear(xn, self.lm_head, None, self.logits[:n], kind="lm_head")

@@ -434,3 +434,70 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
                "rt_silu_mul")
     _count()
     return out
+
+
+# ---------------------------------------------------------------------------
+# tcgen05 projections with fused epilogues (rt_linear)
+# ---------------------------------------------------------------------------
+def linear_supported(m: int, n_out: int, k: int, epilogue: int = 0) -> bool:
+    """Whether rt_linear takes this projection shape."""
+    return _lib.load().rt_linear_check(m, n_out, k, epilogue) == _lib.RT_OK
+
+
+def linear_plan(m: int, n_out: int, k: int, epilogue: int = 0) -> dict:
+    """The launch rt_linear makes for a shape on the current device (K splits, ring stages, smem)."""
+    vals = [ctypes.c_int(0) for _ in range(3)]
+    _lib.check(_lib.load().rt_linear_plan(m, n_out, k, epilogue, *[ctypes.addressof(v) for v in vals]),
+               "rt_linear_plan")
+    return dict(splits=vals[0].value, stages=vals[1].value, smem=vals[2].value)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, epilogue: int = 0,
+           qkv: dict | None = None) -> torch.Tensor | None:
+    """``x [m, k] @ w[n_out, k]^T`` on tcgen05 with an optional fused epilogue (bf16).
+
+    epilogue 0: ``out [m, n_out]``; 1 (w = [gate; up]): ``out [m, n_out/2] =
+    silu(gate) * up``; 2 (w = [Wq; Wk; Wv]): head norms + rotary, q to
+    ``qkv['q_out']``, k/v into the cache (keys of ``qkv`` as in
+    ``qk_norm_rope_append``: num_q_heads, num_kv_heads, q_norm, k_norm, eps,
+    cos, sin, positions, q_out, k_cache, v_cache, offset, offset_dev).
+    """
+    lib = _lib.load()
+    _require_cuda(x, w, out)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(-1) != 1:
+        raise RuntimeError("linear takes bf16 x [m, k] with unit inner stride and bf16 w [n_out, k]")
+    if not w.is_contiguous():
+        raise RuntimeError("linear weights must be contiguous")
+    m, k = x.shape
+    n_out = w.shape[0]
+    if w.shape[1] != k:
+        raise RuntimeError("weight / input inner dimensions differ")
+    dev = x.device
+    if lib.rt_linear_check(m, n_out, k, epilogue) != _lib.RT_OK:
+        raise RuntimeError(f"rt_linear does not take m={m}, n_out={n_out}, k={k}")
+    epi = None
+    keep = []
+    if epilogue == _lib.RT_EPI_QKV_ROPE:
+        kc, vc = qkv["k_cache"], qkv["v_cache"]
+        es = kc.element_size()
+        epi = _lib.QkvEpilogue(qkv["num_q_heads"], qkv["num_kv_heads"], _ptr(qkv.get("q_norm")),
+                               _ptr(qkv.get("k_norm")), float(qkv["eps"]), qkv["cos"].data_ptr(),
+                               qkv["sin"].data_ptr(), qkv["cos"].shape[0], qkv["positions"].data_ptr(),
+                               qkv["q_out"].data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.stride(0) * es,
+                               kc.stride(1) * es, kc.shape[1], int(qkv.get("offset", 0)),
+                               _ptr(qkv.get("offset_dev")))
+        keep.append(epi)
+        out_ptr, ld = None, 0
+    else:
+        if out is None:
+            width = n_out // 2 if epilogue == _lib.RT_EPI_SILU_MUL else n_out
+            out = torch.empty((m, width), dtype=torch.bfloat16, device=dev)
+        if out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+            raise RuntimeError("linear output must be bf16 with unit inner stride")
+        out_ptr, ld = out.data_ptr(), out.stride(0)
+    rc = lib.rt_linear(x.data_ptr(), x.stride(0), m, k, w.data_ptr(), n_out, int(epilogue), out_ptr, ld,
+                       ctypes.addressof(epi) if epi is not None else None, status_tensor(dev).data_ptr(),
+                       _stream(dev))
+    _lib.check(rc, "rt_linear")
+    _count()
+    return out

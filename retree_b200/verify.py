@@ -57,7 +57,8 @@ def extract_context_feature(hidden_states, layer_ids):
 
 class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
-                 temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None):
+                 temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None,
+                 gemm: str = "auto"):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -108,7 +109,7 @@ class TreeVerifier:
             fused = target_layer_ids is None and fused_mod.supports(target)
         if fused and target_layer_ids is not None:
             raise RuntimeError("the fused verify forward does not return hidden states")
-        self.fused = fused_mod.FusedTarget(target, self.cache, self.n_max) if fused else None
+        self.fused = fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm) if fused else None
 
     # ------------------------------------------------------------------ prefill
     @torch.inference_mode()

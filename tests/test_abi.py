@@ -77,3 +77,23 @@ def test_wrappers_refuse_cpu_tensors():
         kernels.draft_topk(x, 2)
     with pytest.raises(RuntimeError, match="CUDA"):
         kernels.kv_compact(torch.zeros(1, 2, 5, 4), 1, torch.zeros(2, dtype=torch.long))
+
+
+def test_qkv_epilogue_struct_layout():
+    import ctypes
+    # int, int, 2 pointers, float (+pad), 2 pointers, int64, 4 pointers, 4 int64, pointer
+    assert ctypes.sizeof(_lib.QkvEpilogue) == 128
+    assert _lib.QkvEpilogue.eps.offset == 24 and _lib.QkvEpilogue.offset_dev.offset == 120
+
+
+def test_linear_shape_checks_without_gpu():
+    lib = _lib.load()
+    # every shape the GPU tests and the Qwen3 projections use has a valid plan (smem within the SM's limit)
+    for m in (1, 17, 33, 40, 65, 200, 257, 300, 512):
+        for n_out, k in ((128, 64), (2560, 4096), (6144, 2560), (19456, 2560), (2560, 9728), (151936, 2560),
+                         (256, 128), (384, 256), (1536, 512)):
+            for epi in (0, 1):
+                assert lib.rt_linear_check(m, n_out, k, epi) == 0, (m, n_out, k, epi)
+    assert lib.rt_linear_check(513, 128, 64, 0) != 0
+    assert lib.rt_linear_check(17, 200, 64, 0) != 0
+    assert lib.rt_linear_check(17, 256, 60, 0) != 0
