@@ -417,6 +417,8 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
+        from retree_b200 import kernels
+        kernels.set_pdl(False)  # NCCL collectives share the stream with the forward's kernels
         log(rank, "process group up")
     try:
         run_ours(args, wl, rank, world, local_rank)

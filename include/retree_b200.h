@@ -51,6 +51,17 @@ int rt_last_cuda_error(void);
 /* Human-readable text for an RT_* or RT_DEV_* code. */
 const char* rt_status_string(int code);
 
+/* Programmatic dependent launch between the kernels of the verify forward
+ * (rt_add_rmsnorm, rt_embed_rmsnorm, rt_qk_norm_rope_append, rt_silu_mul,
+ * rt_linear, rt_tree_attn): each may start its prologue (and its weight or
+ * prefix-KV loads) while the previous kernel in the stream finishes.  On by
+ * default (RETREE_B200_PDL=0 in the environment turns the default off).
+ * Turn it off in processes whose streams also carry NCCL collectives: with
+ * them on the same stream, multi-process rounds were observed to slow down by
+ * orders of magnitude.  Affects launches made after the call. */
+void rt_set_pdl(int enabled);
+int rt_pdl_enabled(void);
+
 /* ------------------------------------------------------------------------
  * KV-cache compaction after a commit.
  * Replaces compact_tail_inplace / _compact_appended_window

@@ -2,20 +2,33 @@
 #include "common.cuh"
 #include "host_util.h"
 
+#include <atomic>
 #include <cstdlib>
 #include <cstring>
 
 namespace rt {
 thread_local int g_last_cuda_error = 0;
 
+namespace {
+std::atomic<int> g_pdl{-1};  // -1: not decided yet (environment), 0 off, 1 on
+}
+
 bool pdl_enabled() {
-  static const bool on = [] {
-    const char* v = std::getenv("RETREE_B200_PDL");
-    return v == nullptr || std::strcmp(v, "0") != 0;
-  }();
-  return on;
+  int v = g_pdl.load(std::memory_order_relaxed);
+  if (v < 0) {
+    const char* e = std::getenv("RETREE_B200_PDL");
+    v = (e == nullptr || std::strcmp(e, "0") != 0) ? 1 : 0;
+    int expected = -1;
+    g_pdl.compare_exchange_strong(expected, v);
+    v = g_pdl.load(std::memory_order_relaxed);
+  }
+  return v != 0;
 }
-}
+}  // namespace rt
+
+extern "C" void rt_set_pdl(int enabled) { rt::g_pdl.store(enabled ? 1 : 0); }
+
+extern "C" int rt_pdl_enabled(void) { return rt::pdl_enabled() ? 1 : 0; }
 
 extern "C" int rt_abi_version(void) { return 2; }
 

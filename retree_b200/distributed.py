@@ -38,6 +38,10 @@ def init(timeout_s: float = 600.0, backend: str | None = None) -> None:
     if backend == "nccl":
         torch.cuda.set_device(local_rank())
     dist.init_process_group(backend=backend, init_method="env://", timeout=datetime.timedelta(seconds=timeout_s))
+    if backend == "nccl":
+        # NCCL collectives on the same streams: no programmatic dependent launch (rt_set_pdl)
+        from . import kernels
+        kernels.set_pdl(False)
 
 
 def is_initialized() -> bool:

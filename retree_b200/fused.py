@@ -160,7 +160,7 @@ class FusedTarget:
             # one decision per process and shape, so every verifier of a model computes alike
             key = (dev.index, self.n_max, self.hidden, self.inter, hq, hkv, self.vocab, len(self.layers))
             if key not in _AUTOTUNE:
-                _AUTOTUNE[key] = self._autotune(self.n_max)
+                _AUTOTUNE[key] = self._agree(self._autotune(self.n_max))
             self.use_rt = dict(_AUTOTUNE[key])
 
     @staticmethod
@@ -189,7 +189,8 @@ class FusedTarget:
         weights stream from HBM as in a round), K/V going to scratch rows.
         """
         dev = self.device
-        x = torch.randn((n, max(self.hidden, self.inter, self.hq * self.head_dim)), device=dev).to(torch.bfloat16)
+        widest = max(w.shape[1] for w in (self.layers[0].qkv_w, self.layers[0].o_w, self.layers[0].down_w))
+        x = torch.randn((n, max(widest, self.hidden)), device=dev).to(torch.bfloat16)
         pos = torch.zeros(n, dtype=torch.int64, device=dev)
         kv = torch.zeros((2, self.hkv, n, self.head_dim), dtype=torch.bfloat16, device=dev)
         choice = {}
@@ -205,14 +206,17 @@ class FusedTarget:
             torch.cuda.synchronize(dev)
             return e0.elapsed_time(e1)
 
+        # (weights, epilogue, bias-free); the input width is the weights' (o_proj
+        # stays full width under a KV-head split)
         specs = {
-            "qkv": ([L.qkv_w for L in self.layers], self.hidden, 2, all(L.qkv_b is None for L in self.layers)),
-            "o": ([L.o_w for L in self.layers], self.hq * self.head_dim, 0, all(L.o_b is None for L in self.layers)),
-            "gate_up": ([L.gate_up_w for L in self.layers], self.hidden, 1, True),
-            "down": ([L.down_w for L in self.layers], self.inter, 0, True),
-            "lm_head": ([self.lm_head], self.hidden, 0, True),
+            "qkv": ([L.qkv_w for L in self.layers], 2, all(L.qkv_b is None for L in self.layers)),
+            "o": ([L.o_w for L in self.layers], 0, all(L.o_b is None for L in self.layers)),
+            "gate_up": ([L.gate_up_w for L in self.layers], 1, True),
+            "down": ([L.down_w for L in self.layers], 0, True),
+            "lm_head": ([self.lm_head], 0, True),
         }
-        for kind, (ws, k, epi, no_bias) in specs.items():
+        for kind, (ws, epi, no_bias) in specs.items():
+            k = ws[0].shape[1]
             xk = x[:, :k]
             if not no_bias or not kernels.linear_supported(n, ws[0].shape[0], k, epi):
                 choice[kind] = False
@@ -242,6 +246,19 @@ class FusedTarget:
             choice[kind] = timed(ours) < timed(library)
         kernels.check_device_status(dev)
         return choice
+
+    def _agree(self, choice: dict) -> dict:
+        """Under a KV-head split the ranks hold replicated activations: take rank 0's choice everywhere."""
+        split = self.layers[0].split
+        if split is None:
+            return choice
+        import torch.distributed as dist
+        group = split[0]
+        kinds = sorted(choice)
+        t = torch.tensor([int(choice[kd]) for kd in kinds], dtype=torch.int32, device=self.device)
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast(t, src=src, group=group)
+        return {kd: bool(v) for kd, v in zip(kinds, t.tolist())}
 
     def _linear(self, x, w, b, out, epilogue: int = 0, kind: str = ""):
         """One projection: rt_linear (tcgen05, fused epilogue) when chosen for this kind, else cuBLAS."""

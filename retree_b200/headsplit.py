@@ -58,6 +58,11 @@ def shard_attention_heads(model, rank: int, world: int, group=None):
         attn.v_proj = _slice_linear(attn.v_proj, slice(k0 * hd, k1 * hd))
         attn._rt_head_split = (group, world, rank)
     model._rt_local_kv_heads = k1 - k0
+    if world > 1 and torch.cuda.is_available():
+        # the forward all-gathers attention outputs on the compute stream: no
+        # programmatic dependent launch around those collectives (rt_set_pdl)
+        from . import kernels
+        kernels.set_pdl(False)
     return model
 
 

@@ -69,6 +69,15 @@ def _count(n: int = 1) -> None:
     LAUNCHES += n
 
 
+def set_pdl(enabled: bool) -> None:
+    """Programmatic dependent launch between the verify-forward kernels (off under NCCL; see rt_set_pdl)."""
+    _lib.load().rt_set_pdl(int(bool(enabled)))
+
+
+def pdl_enabled() -> bool:
+    return bool(_lib.load().rt_pdl_enabled())
+
+
 def status_tensor(device) -> torch.Tensor:
     """The device status word the kernels of this process report into."""
     return _STATE.status(device)
