@@ -39,12 +39,15 @@ class _DeviceState:
         self.lock = threading.Lock()
         self.bufs: dict = {}
 
+    # Buffers are made outside inference mode: they are updated in place from
+    # both inside and outside it (an inference tensor refuses the latter).
     def buffer(self, device, name: str, nbytes: int) -> torch.Tensor:
         key = (torch.device(device).index, name)
         with self.lock:
             b = self.bufs.get(key)
             if b is None or b.numel() < nbytes:
-                b = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
+                with torch.inference_mode(False):
+                    b = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=device)
                 self.bufs[key] = b
             return b
 
@@ -53,7 +56,8 @@ class _DeviceState:
         with self.lock:
             s = self.bufs.get(key)
             if s is None:
-                s = torch.zeros(1, dtype=torch.int32, device=device)
+                with torch.inference_mode(False):
+                    s = torch.zeros(1, dtype=torch.int32, device=device)
                 self.bufs[key] = s
             return s
 
