@@ -414,6 +414,9 @@ def main():
         import torch.distributed as dist
         # the per-step exchanges are tiny all-gathers: no NVLink multicast objects needed
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        # no programmatic dependent launch next to NCCL streams (rt_set_pdl), from the first launch on
+        os.environ["RETREE_B200_PDL"] = "0"
+
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))

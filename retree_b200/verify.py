@@ -106,7 +106,10 @@ class TreeVerifier:
         # verify forward: fused stages (retree_b200.fused) unless the model is not
         # one they cover or the caller needs the HF hidden states
         if fused is None:
-            fused = target_layer_ids is None and fused_mod.supports(target)
+            # (a target split by KV head keeps the module forward: the fused stages
+            # with per-layer all-gathers have not been timed on several GPUs yet)
+            fused = (target_layer_ids is None and fused_mod.supports(target)
+                     and not hasattr(target, "_rt_local_kv_heads"))
         if fused and target_layer_ids is not None:
             raise RuntimeError("the fused verify forward does not return hidden states")
         self.fused = fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm) if fused else None
