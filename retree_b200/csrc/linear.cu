@@ -34,7 +34,6 @@
 // RT_DEV_WAIT_TIMEOUT, drains what it issued, frees TMEM and exits.
 #include <cuda.h>
 
-#include <cstdlib>
 #include <map>
 #include <mutex>
 
@@ -338,15 +337,10 @@ int sm_count() {
   return n;
 }
 
-// 64-column K blocks per ring stage (RETREE_B200_LINEAR_BPS overrides).
-int linear_bps() {
-  static const int v = [] {
-    const char* e = std::getenv("RETREE_B200_LINEAR_BPS");
-    const int b = e ? std::atoi(e) : 1;
-    return (b == 1 || b == 2 || b == 4) ? b : 1;
-  }();
-  return v;
-}
+// 64-column K blocks per ring stage.  One: two and four (longer contiguous
+// runs of each weight row per stage) measured no faster at tree sizes and cost
+// the two-CTAs-per-SM configurations their ring depth.
+int linear_bps() { return 1; }
 
 // CTAs (clusters of `cluster`) of linear_kernel that fit on the GPU at once
 // with `smem` bytes each (cached per shape of the launch).

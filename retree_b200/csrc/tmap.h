@@ -6,7 +6,6 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
-#include <cstdlib>
 
 #include "../../include/retree_b200.h"
 
@@ -31,19 +30,6 @@ inline EncodeTiledFn encode_fn() {
 // Row-major bf16 matrix [rows][cols] (row stride `ld` elements) read in boxes
 // of box_rows x 64 columns with the 128-byte swizzle; out-of-range rows and
 // columns read as zero.
-inline CUtensorMapL2promotion l2_promotion() {
-  static const CUtensorMapL2promotion v = [] {
-    const char* e = std::getenv("RETREE_B200_L2PROMO");
-    switch (e ? std::atoi(e) : 3) {
-      case 0: return CU_TENSOR_MAP_L2_PROMOTION_NONE;
-      case 1: return CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
-      case 2: return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
-      default: return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
-    }
-  }();
-  return v;
-}
-
 inline int make_bf16_2d_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t ld,
                              uint32_t box_rows) {
   EncodeTiledFn fn = encode_fn();
@@ -53,8 +39,8 @@ inline int make_bf16_2d_tmap(CUtensorMap* m, const void* base, int64_t rows, int
   const cuuint32_t box[2] = {64, box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, l2_promotion(),
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? RT_OK : RT_ERR_INVALID_ARGUMENT;
 }
 
