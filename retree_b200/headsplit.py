@@ -1,7 +1,7 @@
 """Split one long request's attention by KV head across ranks.
 
-For a target whose KV cache is too large or too slow for one GPU (BASELINE
-config 5: Qwen3-8B geometry, 32768-token prefix, budget 256), rank g of G keeps
+For a target whose KV cache is too large or too slow for one GPU (e.g. the
+Qwen3-8B geometry with a 32768-token prefix and a 256-node tree), rank g of G keeps
 KV heads ``[g*Hkv/G, (g+1)*Hkv/G)`` and their ``group`` query heads:
 
 * ``shard_attention_heads`` slices every layer's q/k/v projections to the
