@@ -46,11 +46,21 @@ WORKLOADS = {
     # name: model geometry, prompt length, tree budget, draft block
     "qwen3-4b-b16": dict(model="qwen3-4b", prompt=2048, budget=16, block=16),
     "qwen3-4b-b64": dict(model="qwen3-4b", prompt=2048, budget=64, block=16),
-    "qwen3-8b-b64": dict(model="qwen3-8b", prompt=4096, budget=64, block=16),
+    # one request per GPU, request r's prompt length the r-th draw of U[1024, 8192] (seed 0)
+    "qwen3-8b-b64": dict(model="qwen3-8b", prompt=(1024, 8192), budget=64, block=16),
     # one long request split by KV head over the ranks (random N(0,1) KV prefix, no prompt forward)
     "qwen3-8b-l32k-b256-split": dict(model="qwen3-8b", prompt=32768, budget=256, block=16, split=True),
 }
 DELTA_PAIRS = 4096  # recovery-memory delta exchanged per step at N>1 (int32 draft, target, count)
+
+
+def prompt_len(wl: dict, req: int) -> int:
+    """Prompt length of request ``req``: fixed, or the req-th seeded draw of a uniform range."""
+    p = wl["prompt"]
+    if isinstance(p, int):
+        return p
+    lo, hi = p
+    return int(np.random.default_rng(0).integers(lo, hi + 1, size=max(8, req + 1))[req])
 
 
 def parse():
@@ -137,7 +147,7 @@ def cpu_round_sample(cfg, wl, rounds: int, strategy: str):
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    r = CpuVerifyRound(cfg, wl["prompt"], wl["budget"], strategy=strategy, params=NgramParams())
+    r = CpuVerifyRound(cfg, prompt_len(wl, 0), wl["budget"], strategy=strategy, params=NgramParams())
     drafts = [draft_logits_np(1000 + i, wl["block"], cfg.vocab_size) for i in range(rounds + 1)]
     r.round(drafts[0])  # warm-up
     t0 = time.perf_counter()
@@ -157,7 +167,7 @@ def run_reference(args, wl, rank, world):
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
-    r = CpuVerifyRound(cfg, wl["prompt"], wl["budget"], strategy=args.strategy, params=NgramParams())
+    r = CpuVerifyRound(cfg, prompt_len(wl, 0), wl["budget"], strategy=args.strategy, params=NgramParams())
     drafts = [draft_logits_np(1000 + i, wl["block"], cfg.vocab_size) for i in range(args.warmup + args.steps)]
     for i in range(args.warmup):
         r.round(drafts[i])
@@ -173,7 +183,7 @@ def run_reference(args, wl, rank, world):
         "impl": "reference", "metric": "verify rounds/sec", "value": value, "unit": "rounds/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.workload, "model": wl["model"], "prompt": wl["prompt"], "budget": wl["budget"],
+        "config": {"workload": args.workload, "model": wl["model"], "prompt": prompt_len(wl, 0), "budget": wl["budget"],
                    "draft_block": wl["block"], "strategy": args.strategy, "parallelism": "host CPU, rank 0 only"},
         "cpu_baseline": {"value": value, "unit": "rounds/s", "cores": cores, "kind": "port", "sample": sample},
         "e2e": {"value": value, "unit": "rounds/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -212,25 +222,30 @@ def run_ours(args, wl, rank, world, local_rank):
     log(rank, "target built")
     steps, warm = args.steps, args.warmup
     total_rounds = warm + steps
-    max_len = wl["prompt"] + total_rounds * (wl["block"] + 2) + 64
-    # draft logits for every round: bf16 as the lm_head emits them; pinned host copies for the e2e leg
     req = 0 if wl.get("split") else rank  # a split request is the same request on every rank
+    plen = prompt_len(wl, req)
+    max_len = plen + total_rounds * (wl["block"] + 2) + 64
+    # draft logits for every round: bf16 as the lm_head emits them; pinned host copies for the e2e leg
     host = [torch.from_numpy(draft_logits_np(1000 + 7919 * req + i, wl["block"], cfg.vocab_size)).to(torch.bfloat16)
             for i in range(total_rounds)]
     pinned = [h.pin_memory() for h in host]
     resident = [h.to(dev) for h in host]
-    prompt = torch.from_numpy(np.random.default_rng(req).integers(0, cfg.vocab_size, size=wl["prompt"]))[None]
+    prompt = torch.from_numpy(np.random.default_rng(req).integers(0, cfg.vocab_size, size=plen))[None]
 
     def fresh():
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
                          fused=not args.hf_forward, gemm=args.gemm)
         if wl.get("split"):
-            v.prefill_random(wl["prompt"], seed=req)
+            v.prefill_random(plen, seed=req)
         else:
             v.prefill(prompt.to(dev))
         return v
 
-    delta_send = torch.zeros((DELTA_PAIRS, 3), dtype=torch.int32, device=dev)
+    # the step's recovery-memory delta: seeded random (draft, target) pairs and counts
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    delta_send = torch.stack([torch.randint(0, cfg.vocab_size, (DELTA_PAIRS,), device=dev, generator=g),
+                              torch.randint(0, cfg.vocab_size, (DELTA_PAIRS,), device=dev, generator=g),
+                              torch.randint(1, 5, (DELTA_PAIRS,), device=dev, generator=g)], dim=1).to(torch.int32)
     delta_recv = torch.zeros((world, DELTA_PAIRS, 3), dtype=torch.int32, device=dev) if world > 1 else None
 
     def exchange():
@@ -379,7 +394,8 @@ def run_ours(args, wl, rank, world, local_rank):
         "scaling": "strong" if wl.get("split") else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded draft logits, uniform prompt, random-init "
                                                       "weights)",
-        "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": wl["prompt"],
+        "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": plen,
+                   "prompt_lengths": [prompt_len(wl, 0 if wl.get("split") else r) for r in range(world)],
                    "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
                    "projections": projections,
