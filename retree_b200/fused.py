@@ -42,6 +42,7 @@ import torch
 from torch import nn
 
 from . import kernels
+from .headsplit import gather_heads
 
 SUPPORTED_MODEL_TYPES = ("qwen3", "qwen2", "llama")
 
@@ -320,7 +321,6 @@ class FusedTarget:
                                        scale=L.scale, out=self.attn[:n], num_splits=splits, kv_capacity=cap)
             attn = self.attn[:n]
             if L.split is not None:
-                from .headsplit import gather_heads
                 group, world, _ = L.split
                 attn = gather_heads(attn.unsqueeze(0), group, world)[0]
             self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n], kind="o")
