@@ -1,0 +1,99 @@
+"""Recovery memory as a device hash table for the on-device recovery walk.
+
+Layout shared with ``csrc/recovery_walk.cuh``: open addressing with linear
+probing over a power-of-two capacity, key ``draft << 32 | target`` (uint64,
+all ones = empty), slot = splitmix64-mix(key) & (capacity - 1), and separate
+int32 prior / online count arrays (the two tables of RecoveryMemory,
+model/recovery.py:35-266).  ``RecoveryTable`` builds and reads the table on
+the host (numpy); ``to_device`` hands the three arrays to torch.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+from .recovery import RecoveryMemory
+
+EMPTY = np.uint64(0xFFFFFFFFFFFFFFFF)
+_M1 = np.uint64(0xBF58476D1CE4E5B9)
+_M2 = np.uint64(0x94D049BB133111EB)
+
+
+def mix64(x) -> np.uint64:
+    """splitmix64's output mix (Steele, Lea, Flood 2014), wrapping uint64 arithmetic."""
+    x = np.uint64(x)
+    with np.errstate(over="ignore"):
+        x ^= x >> np.uint64(30)
+        x = np.uint64(x * _M1)
+        x ^= x >> np.uint64(27)
+        x = np.uint64(x * _M2)
+        x ^= x >> np.uint64(31)
+    return x
+
+
+def pair_key(draft: int, target: int) -> np.uint64:
+    return np.uint64(((int(draft) & 0xFFFFFFFF) << 32) | (int(target) & 0xFFFFFFFF))
+
+
+class RecoveryTable:
+    def __init__(self, capacity: int):
+        if capacity <= 0 or capacity & (capacity - 1):
+            raise ValueError("capacity must be a power of two")
+        self.capacity = int(capacity)
+        self.keys = np.full(self.capacity, EMPTY, dtype=np.uint64)
+        self.prior = np.zeros(self.capacity, dtype=np.int32)
+        self.online = np.zeros(self.capacity, dtype=np.int32)
+
+    @staticmethod
+    def capacity_for(pairs: int, load: float = 0.5, minimum: int = 1 << 12) -> int:
+        need = max(minimum, int(math.ceil(max(pairs, 1) / load)))
+        return 1 << (need - 1).bit_length()
+
+    @classmethod
+    def from_memory(cls, memory: RecoveryMemory, capacity: int | None = None, extra_pairs: int = 1 << 16):
+        pairs = set(memory.prior_counts()) | set(memory.online_counts())
+        t = cls(capacity or cls.capacity_for(len(pairs) + extra_pairs))
+        for (d, g), c in memory.prior_counts().items():
+            t.prior[t.insert(d, g)] += c
+        for (d, g), c in memory.online_counts().items():
+            t.online[t.insert(d, g)] += c
+        return t
+
+    def _slot(self, key: np.uint64, insert: bool) -> int:
+        mask = self.capacity - 1
+        s = int(mix64(key)) & mask
+        for _ in range(self.capacity):
+            k = self.keys[s]
+            if k == key:
+                return s
+            if k == EMPTY:
+                if not insert:
+                    return -1
+                self.keys[s] = key
+                return s
+            s = (s + 1) & mask
+        if insert:
+            raise RuntimeError("recovery table full")
+        return -1
+
+    def insert(self, draft: int, target: int) -> int:
+        return self._slot(pair_key(draft, target), True)
+
+    def frequency(self, draft: int, target: int) -> int:
+        s = self._slot(pair_key(draft, target), False)
+        return 0 if s < 0 else int(self.prior[s]) + int(self.online[s])
+
+    def online_counts(self) -> dict:
+        used = (self.keys != EMPTY) & (self.online > 0)
+        out = {}
+        for k, c in zip(self.keys[used].tolist(), self.online[used].tolist()):
+            d, g = k >> 32, k & 0xFFFFFFFF
+            out[(d - (1 << 32) if d >= 1 << 31 else d, g - (1 << 32) if g >= 1 << 31 else g)] = c
+        return out
+
+    def to_device(self, device):
+        import torch
+        return (torch.from_numpy(self.keys.view(np.int64)).to(device), torch.from_numpy(self.prior).to(device),
+                torch.from_numpy(self.online).to(device))

@@ -18,12 +18,16 @@ from .recovery import RecoveryMemory, target_logit_consistency_gate, token_pair_
 
 
 def _rank_children_by_target_logits(children: dict[int, int], logits_2d: torch.Tensor, position: int):
-    """Children ``(token, node)`` by descending target logit at ``position`` (retree.py:25-54)."""
+    """Children ``(token, node)`` by descending target logit at ``position`` (retree.py:25-54).
+
+    Equal logits keep the children's dict order (a stable sort; the reference's
+    unstable argsort leaves their order to the sort implementation).
+    """
     if not children:
         return []
     toks = torch.tensor([int(t) for t in children.keys()], dtype=torch.long, device=logits_2d.device)
     scores = logits_2d[position].index_select(0, toks)
-    order = torch.argsort(scores, descending=True).tolist()
+    order = torch.argsort(scores, descending=True, stable=True).tolist()
     toks_host = toks.tolist()
     return [(toks_host[j], children[toks_host[j]]) for j in order]
 
