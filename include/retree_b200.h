@@ -252,6 +252,46 @@ int rt_tree_walk(const int32_t* parents, const int64_t* node_tokens, int count, 
                  int* status, rt_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * Target-gated sibling-recovery walk on the device.
+ * Replaces follow_verified_tree_with_recovery (retree.py:57-190) with the
+ * RecoveryMemory reads and online updates it makes (model/recovery.py:35-298,
+ * the gate :283-298, the stop check :269-280); no host syncs.
+ *
+ * The tree is given as in rt_tree_walk (parents int32[count+1], node tokens
+ * int64[count], count from count_dev when non-NULL, <= the host count, which
+ * is at most 1023).  posterior int64[count+1]; logits [count+1, >= vocab]
+ * (row stride logits_ld elements, dtype 0 fp32 / 1 bf16: the gate
+ * logit[draft] - logit[target] >= log(gate_threshold) is evaluated in that
+ * dtype; gate_threshold <= 0 turns it off).  Walk: follow the child whose
+ * token is the target's; at a mismatch (target not a stop id) rank the
+ * children by target logit (ties in first-occurrence order), snapshot the
+ * pair frequencies (prior + online) of the first rescue_top_k, add one online
+ * count for each of the first record_top_k ranked children that differ from
+ * the target (when online_update; stop pairs skipped), then move to the first
+ * candidate whose snapshot frequency is >= freq_threshold and that passes the
+ * gate; stop when none does.  stop_ids (int64[n_stop], DEVICE) is the
+ * reference's disallow_rescue_target_ids; NULL means none.
+ *
+ * Recovery memory: open-addressing table of table_capacity (a power of two)
+ * slots, key uint64 = draft << 32 | target (all ones = empty), slot =
+ * splitmix64-mix(key) & (capacity - 1) with linear probing, prior / online
+ * int32 counts per slot (retree_b200/recovery_device.py builds it).  Each
+ * online increment is also appended as (draft, target) int32 to log_pairs at
+ * *log_count (both may be NULL), up to log_capacity (RT_DEV_OVERFLOW beyond).
+ * Outputs accepted / accepted_len / next_token as rt_tree_walk, rescued =
+ * number of sibling rescues; output_ids / start_dev commit as in
+ * rt_tree_walk when non-NULL.
+ * ---------------------------------------------------------------------- */
+int rt_recovery_walk(const int32_t* parents, const int64_t* node_tokens, int count, const int32_t* count_dev,
+                     const int64_t* posterior, const void* logits, int64_t logits_ld, int logits_dtype,
+                     int64_t vocab, double gate_threshold, int64_t freq_threshold, int rescue_top_k,
+                     int record_top_k, int online_update, const int64_t* stop_ids, int n_stop, void* table_keys,
+                     int32_t* table_prior, int32_t* table_online, int64_t table_capacity, int32_t* log_pairs,
+                     int32_t* log_count, int log_capacity, int64_t* accepted, int32_t* accepted_len,
+                     int64_t* next_token, int32_t* rescued, const int64_t* verify_ids, int64_t* output_ids,
+                     int64_t output_len, int64_t* start_dev, int* status, rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * Elementwise stages of the target's verify forward (bf16, row-major,
  * contiguous, 16-byte aligned rows).  Each reproduces the bf16 rounding
  * points of the transformers ops it replaces; the projections between them

@@ -42,6 +42,8 @@ SIGNATURES = {
     "rt_tree_build": (_I, [_P, _P, _I, _I, _I, _I, _P, _I64, _P, _I, _I, _D, _I, _I, _I, _P, _D, _P, _I,
                            _P, _P, _P, _P, _I, _P, _P, _P, _I64, _P, _I64, _P, _P, _P]),
     "rt_tree_walk": (_I, [_P, _P, _I, _P, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P]),
+    "rt_recovery_walk": (_I, [_P, _P, _I, _P, _P, _P, _I64, _I, _I64, _D, _I64, _I, _I, _I, _P, _I, _P, _P, _P,
+                              _I64, _P, _P, _I, _P, _P, _P, _P, _P, _P, _I64, _P, _P, _P]),
     "rt_embed_rmsnorm": (_I, [_P, _P, _I64, _P, _P, _P, _I, _I, _F, _P, _P]),
     "rt_add_rmsnorm": (_I, [_P, _P, _P, _P, _I, _I, _F, _P]),
     "rt_qk_norm_rope_append": (_I, [_P, _I, _I, _I, _I, _P, _P, _F, _P, _P, _I64, _P, _P, _P, _P, _I64, _I64,

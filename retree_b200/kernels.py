@@ -514,3 +514,50 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ep
     _lib.check(rc, "rt_linear")
     _count()
     return out
+
+
+# ---------------------------------------------------------------------------
+# Target-gated sibling-recovery walk (rt_recovery_walk)
+# ---------------------------------------------------------------------------
+def recovery_walk(parents: torch.Tensor, tokens: torch.Tensor, posterior: torch.Tensor, logits: torch.Tensor,
+                  table: tuple, params: dict, count: int | None = None, count_dev: torch.Tensor | None = None,
+                  stop_ids: torch.Tensor | None = None, log: tuple | None = None, out: dict | None = None,
+                  verify_ids: torch.Tensor | None = None, output_ids: torch.Tensor | None = None,
+                  start_dev: torch.Tensor | None = None) -> dict:
+    """ReTree's recovery walk on the device.
+
+    ``table`` = (keys int64[cap], prior int32[cap], online int32[cap]) of
+    ``recovery_device.RecoveryTable``; ``params`` = gate_threshold,
+    freq_threshold, rescue_top_k, record_top_k, online_update; ``log`` =
+    (pairs int32[cap, 2], count int32[1]) or None; ``stop_ids`` int64 or None
+    (no stop set).  Returns ``out`` with accepted / accepted_len / next_token /
+    rescued.
+    """
+    _require_cuda(parents, tokens, posterior, logits, stop_ids, verify_ids, output_ids, start_dev, *table)
+    dev = parents.device
+    n_max = parents.numel()
+    cnt = n_max - 1 if count is None else int(count)
+    if logits.dtype not in (torch.float32, torch.bfloat16) or logits.dim() != 2 or logits.stride(-1) != 1:
+        raise RuntimeError("logits must be [nodes, vocab] fp32 or bf16 with contiguous rows")
+    if out is None:
+        out = dict(accepted=torch.zeros(n_max, dtype=torch.int64, device=dev),
+                   accepted_len=torch.zeros(1, dtype=torch.int32, device=dev),
+                   next_token=torch.zeros(1, dtype=torch.int64, device=dev),
+                   rescued=torch.zeros(1, dtype=torch.int32, device=dev))
+    keys, prior, online = table
+    log_pairs, log_count = (None, None) if log is None else log
+    rc = _lib.load().rt_recovery_walk(
+        parents.data_ptr(), _ptr(tokens), cnt, _ptr(count_dev), posterior.data_ptr(), logits.data_ptr(),
+        logits.stride(0), 0 if logits.dtype == torch.float32 else 1, logits.shape[1],
+        float(params.get("gate_threshold", 0.01)), int(params.get("freq_threshold", 6)),
+        int(params.get("rescue_top_k", 8)), int(params.get("record_top_k", 8)),
+        int(bool(params.get("online_update", True))), _ptr(stop_ids),
+        0 if stop_ids is None else stop_ids.numel(), keys.data_ptr(), prior.data_ptr(), online.data_ptr(),
+        keys.numel(), _ptr(log_pairs), _ptr(log_count), 0 if log_pairs is None else log_pairs.shape[0],
+        out["accepted"].data_ptr(), out["accepted_len"].data_ptr(), out["next_token"].data_ptr(),
+        out["rescued"].data_ptr(), _ptr(verify_ids), _ptr(output_ids),
+        0 if output_ids is None else output_ids.numel(), _ptr(start_dev), status_tensor(dev).data_ptr(),
+        _stream(dev))
+    _lib.check(rc, "rt_recovery_walk")
+    _count()
+    return out

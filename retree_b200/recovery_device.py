@@ -97,3 +97,58 @@ class RecoveryTable:
         import torch
         return (torch.from_numpy(self.keys.view(np.int64)).to(device), torch.from_numpy(self.prior).to(device),
                 torch.from_numpy(self.online).to(device))
+
+
+class DeviceRecoveryMemory:
+    """A RecoveryMemory whose counts live in a device table that the recovery walk updates in place.
+
+    ``memory`` (the host RecoveryMemory) stays the record for files and the
+    cross-rank delta exchange: ``sync()`` applies the walk's logged online
+    increments to it.  The log holds ``log_capacity`` increments between syncs.
+    """
+
+    def __init__(self, memory: RecoveryMemory, device, capacity: int | None = None, log_capacity: int = 1 << 16,
+                 stop_ids=None):
+        import torch
+        self.memory = memory
+        self.device = torch.device(device)
+        host = RecoveryTable.from_memory(memory, capacity)
+        self.capacity = host.capacity
+        self.table = host.to_device(self.device)
+        self.log_pairs = torch.zeros((log_capacity, 2), dtype=torch.int32, device=self.device)
+        self.log_count = torch.zeros(1, dtype=torch.int32, device=self.device)
+        # an empty stop set behaves as none (no pair is a stop pair)
+        stops = sorted({int(t) for t in stop_ids}) if stop_ids is not None else []
+        self.stop_ids = torch.tensor(stops, dtype=torch.int64, device=self.device) if stops else None
+
+    @property
+    def freq_threshold(self) -> int:
+        return self.memory.freq_threshold
+
+    def log(self):
+        return self.log_pairs, self.log_count
+
+    def sync(self) -> int:
+        """Apply the logged online increments to the host memory; returns how many."""
+        n = int(self.log_count.item())
+        if n:
+            for d, t in self.log_pairs[:n].cpu().tolist():
+                self.memory.record_online(d, t)
+            self.log_count.zero_()
+        return n
+
+    def apply_online_delta(self, delta: dict) -> None:
+        """Other ranks' online counts (distributed.synchronize_online_memory), on both copies."""
+        if not delta:
+            return
+        self.memory.apply_online_delta(delta)
+        keys, prior, online = self.table
+        host = RecoveryTable(self.capacity)
+        host.keys[:] = keys.cpu().numpy().view(np.uint64)
+        host.prior[:] = prior.cpu().numpy()
+        host.online[:] = online.cpu().numpy()
+        for (d, t), c in delta.items():
+            host.online[host.insert(d, t)] += int(c)
+        # in place: CUDA graphs captured over the walk keep the same buffers
+        for dst, src in zip(self.table, host.to_device(self.device)):
+            dst.copy_(src)
