@@ -88,8 +88,13 @@ def retree_generate(model, target, input_ids, mask_token_id, max_new_tokens, blo
                     temperature: float = 0.0, tree_budget: int | None = None,
                     recovery_memory: RecoveryMemory | None = None, gate_threshold: float = 0.01,
                     recovery_online_update: bool = True, recovery_record_top_k: int = 8,
-                    recovery_rescue_top_k: int = 8, draft_fn=None):
-    """ReTree decode loop (retree.py:193-444); ``total_rescued`` counts sibling rescues."""
+                    recovery_rescue_top_k: int = 8, draft_fn=None, device_recovery: bool = False):
+    """ReTree decode loop (retree.py:193-444); ``total_rescued`` counts sibling rescues.
+
+    ``device_recovery`` runs the recovery walk on the GPU (rt_recovery_walk)
+    over a device copy of ``recovery_memory``; its online counts are applied to
+    ``recovery_memory`` when the request ends.
+    """
     from .verify import TreeVerifier
 
     if block_size <= 1:
@@ -108,6 +113,16 @@ def retree_generate(model, target, input_ids, mask_token_id, max_new_tokens, blo
     verifier = TreeVerifier(target, tree_budget=(block_size - 1) if tree_budget is None else max(tree_budget, 0),
                             max_length=input_ids.shape[1] + max_new_tokens + 2 * block_size + 8,
                             draft_horizon=block_size - 1, temperature=temperature)
+    if device_recovery and recovery_memory is not None:
+        from .recovery_device import DeviceRecoveryMemory
+        dm = DeviceRecoveryMemory(recovery_memory, verifier.device, stop_ids=stop_set)
+        verifier.enable_recovery(dm, gate_threshold=gate_threshold, rescue_top_k=recovery_rescue_top_k,
+                                 record_top_k=recovery_record_top_k, online_update=recovery_online_update)
+        out = verifier.generate(input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
+                                draft_model=model, draft_fn=draft_fn)
+        dm.sync()
+        out.total_rescued = int(verifier.rescued_total.item())
+        return out
     out = verifier.generate(input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
                             draft_model=model, draft_fn=draft_fn,
                             host_walk=None if recovery_memory is None else walk)

@@ -98,7 +98,12 @@ class TreeVerifier:
         )
         self.walk = dict(accepted=torch.zeros(self.n_max, dtype=torch.int64, device=d),
                          accepted_len=torch.zeros(1, dtype=torch.int32, device=d),
-                         next_token=torch.zeros(1, dtype=torch.int64, device=d))
+                         next_token=torch.zeros(1, dtype=torch.int64, device=d),
+                         rescued=torch.zeros(1, dtype=torch.int32, device=d))
+        # ReTree's sibling recovery on the device (enable_recovery); None = exact walk
+        self.recovery = None
+        self.recovery_params: dict = {}
+        self.rescued_total = torch.zeros(1, dtype=torch.int64, device=d)
         self.stage_times = empty_stage_times(DDTREE_STAGE_ORDER + DDTREE_TREE_BUILD_STAGE_ORDER)
         self.timed = False
         self.debug = False  # keep the posterior and the pre-compaction cache of the last round
@@ -176,6 +181,32 @@ class TreeVerifier:
         if self.graph_mode:
             self.cache.length_dev = self.start_dev[:1]
 
+    def enable_recovery(self, memory, gate_threshold: float = 0.01, rescue_top_k: int = 8, record_top_k: int = 8,
+                        online_update: bool = True) -> None:
+        """Walk with ReTree's target-gated sibling recovery on the device (rt_recovery_walk).
+
+        ``memory`` is a ``recovery_device.DeviceRecoveryMemory`` (None: back to
+        the exact walk); the knobs are those of follow_verified_tree_with_recovery.
+        """
+        self.recovery = memory
+        self.recovery_params = dict(gate_threshold=gate_threshold, rescue_top_k=rescue_top_k,
+                                    record_top_k=record_top_k, online_update=online_update,
+                                    freq_threshold=0 if memory is None else memory.freq_threshold)
+        self.graph = None
+
+    def _walk_and_commit(self, posterior: torch.Tensor, logits: torch.Tensor, count: int) -> None:
+        """Exact or recovery walk over the round's tree; commits to the output ids and start_dev."""
+        if self.recovery is None:
+            kernels.tree_walk(self.tree["parents"], self.tree["tokens"], posterior, count=count, out=self.walk,
+                              verify_ids=self.tree["verify_ids"], output_ids=self.output_ids,
+                              start_dev=self.start_dev)
+            return
+        kernels.recovery_walk(self.tree["parents"], self.tree["tokens"], posterior, logits, self.recovery.table,
+                              self.recovery_params, count=count, stop_ids=self.recovery.stop_ids,
+                              log=self.recovery.log(), out=self.walk, verify_ids=self.tree["verify_ids"],
+                              output_ids=self.output_ids, start_dev=self.start_dev)
+        self.rescued_total += self.walk["rescued"]
+
     def _round_body(self, logits: torch.Tensor, count: int) -> None:
         """One round with every varying quantity on the device (capturable)."""
         n = 1 + count
@@ -194,8 +225,7 @@ class TreeVerifier:
             logits = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache,
                                  use_cache=True).logits
         posterior = sample(logits, self.temperature)
-        kernels.tree_walk(self.tree["parents"], self.tree["tokens"], posterior[0], count=count, out=self.walk,
-                          verify_ids=self.tree["verify_ids"], output_ids=self.output_ids, start_dev=self.start_dev)
+        self._walk_and_commit(posterior[0], logits[0], count)
         kernels.kv_compact(self.cache.slab, 0, self.walk["accepted"], cur_length=n,
                            n_keep_dev=self.walk["accepted_len"], n_keep=n, past_len_dev=self.start_dev[1:2])
 
@@ -275,9 +305,7 @@ class TreeVerifier:
             self.last_posterior = posterior
             self.last_slab = self.cache.slab[:, :, : start + n, :].clone()
         if host_walk is None:
-            kernels.tree_walk(self.tree["parents"], self.tree["tokens"], posterior[0], count=count,
-                              out=self.walk, verify_ids=self.tree["verify_ids"], output_ids=self.output_ids,
-                              start_dev=self.start_dev)
+            self._walk_and_commit(posterior[0], out.logits[0], count)
             kernels.kv_compact(self.cache.slab[:, :, : start + n, :], start, self.walk["accepted"], cur_length=n,
                                n_keep_dev=self.walk["accepted_len"], n_keep=n)
             acc_len = int(self.walk["accepted_len"].item())
