@@ -23,7 +23,6 @@ tokens) -- the reference syncs several times per round (ddtree.py:361-367,
 
 from __future__ import annotations
 
-import time
 from types import SimpleNamespace
 
 import torch

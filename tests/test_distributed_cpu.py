@@ -103,7 +103,6 @@ def test_single_process_fallbacks():
 
 
 def _headsplit_forward(r, world):
-    import numpy as np
     import torch
     from oracle import tree as ot
     from retree_b200 import headsplit, synthetic

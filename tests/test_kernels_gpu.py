@@ -7,7 +7,7 @@ import torch
 from oracle import tree as ot
 from retree_b200 import kernels
 from tests import golden_cases as gc
-from tests.gpu_util import bits_tensor, cuda
+from tests.gpu_util import cuda
 
 pytestmark = pytest.mark.gpu
 

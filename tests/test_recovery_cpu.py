@@ -9,7 +9,6 @@ import json
 import tempfile
 from pathlib import Path
 
-import numpy as np
 import torch
 
 from oracle import tree as ot

@@ -1,7 +1,6 @@
 """The drop-in API on a real (small, random) Qwen3 target: backend vs SDPA, cache compaction,
 verifier rounds stage by stage against the oracle, and tree decoding == greedy decoding."""
 
-import os
 
 import numpy as np
 import pytest

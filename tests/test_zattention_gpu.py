@@ -4,7 +4,6 @@ Tolerance (the north-star bound for this path): max |err| <= 2e-2 and
 mean |err| <= 1e-3 against fp32 attention on the same bf16-rounded inputs.
 """
 
-import numpy as np
 import pytest
 import torch
 
