@@ -104,40 +104,85 @@ def profile_traffic(workload: str):
     return float(m.group(1)) if m else None
 
 
-class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+CLOCK_QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+REASONS = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, index: int):
+
+def summarize_clocks(lines: list[str], t0: float, t1: float, interval_s: float) -> dict:
+    """Median SM clock and active throttle reasons of the samples taken during [t0, t1].
+
+    ``lines`` are nvidia-smi CSV rows of CLOCK_QUERY (timestamp first, local
+    time); a sample within one interval of the region counts as taken during
+    it.  With none there, the sample nearest the region stands in
+    (``samples_in_region`` 0).
+    """
+    rows = []
+    for line in lines:
+        r = [x.strip() for x in line.split(",")]
+        if len(r) < 10:
+            continue
+        try:
+            sm, sm_max = float(r[2]), float(r[3])
+        except ValueError:
+            continue
+        try:
+            ts = datetime.datetime.strptime(r[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+        except ValueError:
+            ts = None
+        rows.append((ts, sm, sm_max, r[6:10]))
+    if not rows:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+    timed_rows = [x for x in rows if x[0] is not None]
+    if not timed_rows:  # unreadable timestamps: every sample counts, as before the region was marked
+        inside, use = [], rows
+    else:
+        inside = [x for x in timed_rows if t0 - interval_s <= x[0] <= t1 + interval_s]
+        use = inside or [min(timed_rows, key=lambda x: min(abs(x[0] - t0), abs(x[0] - t1)))]
+    reasons = sorted({REASONS[i] for x in use for i in range(4) if x[3][i] == "Active"})
+    return {"sm_mhz": statistics.median(x[1] for x in use), "sm_max_mhz": use[0][2], "reasons": reasons,
+            "samples": len(rows), "samples_in_region": len(inside)}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons, sampled every ``interval_ms`` from before the timed
+    region (so that sampling is running when it starts) and summarised over the region."""
+
+    def __init__(self, index: int, interval_ms: int = 20):
         vis = os.environ.get("CUDA_VISIBLE_DEVICES")
         if vis:
             ids = [x.strip() for x in vis.split(",") if x.strip()]
             if index < len(ids) and ids[index].isdigit():
                 index = int(ids[index])
+        self.interval_s = interval_ms / 1000.0
+        self.t0 = self.t1 = None
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
-            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "200"], stdout=self.f, stderr=subprocess.DEVNULL)
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={index}", f"--query-gpu={CLOCK_QUERY}",
+                                       "--format=csv,noheader,nounits", "-lms", str(interval_ms)],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.p = None
+
+    def mark_start(self) -> None:
+        self.t0 = time.time()
+
+    def mark_end(self) -> None:
+        self.t1 = time.time()
 
     def stop(self) -> dict:
         if self.p is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(2 * self.interval_s)  # a sample after the region's end
         self.p.terminate()
         self.p.wait()
         self.f.seek(0)
-        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        lines = self.f.read().strip().splitlines()
         os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
-                "samples": len(rows)}
+        t1 = self.t1 if self.t1 is not None else time.time()
+        t0 = self.t0 if self.t0 is not None else t1
+        return summarize_clocks(lines, t0, t1, self.interval_s)
 
 
 def cpu_round_sample(cfg, wl, rounds: int, strategy: str):
@@ -271,12 +316,12 @@ def run_ours(args, wl, rank, world, local_rank):
     # ---- device-resident rounds (value): every round is one CUDA-graph replay ----
     v = fresh()
     v.enable_graph(not args.eager)
+    sampler = ClockSampler(dev.index) if rank == 0 else None  # running before the timed region starts
     for i in range(warm):
         v.round(resident[i])
         exchange()
     log(rank, "warm-up rounds done")
     kernels.LAUNCHES = 0
-    sampler = ClockSampler(dev.index) if rank == 0 else None
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     accepted = []
 
@@ -289,7 +334,11 @@ def run_ours(args, wl, rank, world, local_rank):
         ev1.record()
         torch.cuda.nvtx.range_pop()
 
+    if sampler:
+        sampler.mark_start()
     wall = timed(rounds_resident)
+    if sampler:
+        sampler.mark_end()
     clocks = sampler.stop() if sampler else None
     launches = kernels.LAUNCHES
     torch.cuda.synchronize()
