@@ -137,8 +137,9 @@ def _tree(seed, n, L, dev):
 
 
 @torch.inference_mode()
-@pytest.mark.parametrize("device_offset", [False, True])
-def test_fused_forward_matches_hf_forward(device_offset):
+@pytest.mark.parametrize("device_offset,gemm", [(False, "auto"), (True, "auto"), (False, "tcgen05"),
+                                                (True, "cublas")])
+def test_fused_forward_matches_hf_forward(device_offset, gemm):
     dev = cuda()
     model = build_target(_cfg(3), device=dev, seed=5)
     L = 260
@@ -152,7 +153,7 @@ def test_fused_forward_matches_hf_forward(device_offset):
     tok = torch.randint(0, VOCAB, (n,), device=dev, generator=torch.Generator(device=dev).manual_seed(9))
     want = model(tok[None], position_ids=pos[None], attention_mask=attention.attach(bits.view(1, 1, n, -1), bits),
                  past_key_values=c_hf, use_cache=True).logits[0]
-    ft = fused.FusedTarget(model, c_fu, n_max=64)
+    ft = fused.FusedTarget(model, c_fu, n_max=64, gemm=gemm)
     if device_offset:
         got = ft.forward(tok, pos, bits, offset_dev=torch.tensor([L], dtype=torch.int64, device=dev)).clone()
     else:
