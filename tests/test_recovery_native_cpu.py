@@ -172,3 +172,35 @@ def test_device_table_layout_matches_host_lookup():
     for (d, g) in [(1, 2), (5, 2), (2 ** 31 - 1, 7), (0, 0), (9, 9)]:
         assert t.frequency(d, g) == mem.get_frequency(d, g)
     assert t.online_counts() == {(1, 2): 2}
+
+
+def test_device_memory_host_logic_on_cpu_tensors():
+    """DeviceRecoveryMemory's host side: table build, log sync into the host memory, delta application."""
+    from retree_b200.recovery_device import DeviceRecoveryMemory
+
+    mem = RecoveryMemory(2)
+    mem.record_prior(3, 4, 5)
+    mem.record_online(3, 4, 1)
+    dm = DeviceRecoveryMemory(mem, "cpu", capacity=64, log_capacity=8, stop_ids={7, 9})
+    assert dm.stop_ids.tolist() == [7, 9] and dm.freq_threshold == 2
+    keys, prior, online = dm.table
+    host = RecoveryTable(64)
+    host.keys[:] = keys.numpy().view(np.uint64)
+    host.prior[:] = prior.numpy()
+    host.online[:] = online.numpy()
+    assert host.frequency(3, 4) == 6 and host.frequency(4, 3) == 0
+    # the walk's log: two increments of (10, 11), one of (3, 4)
+    dm.log_pairs[:3] = torch.tensor([[10, 11], [3, 4], [10, 11]], dtype=torch.int32)
+    dm.log_count.fill_(3)
+    assert dm.sync() == 3 and int(dm.log_count.item()) == 0
+    assert mem.online_counts() == {(3, 4): 2, (10, 11): 2}
+    # another rank's delta lands in both copies, in place
+    keys_ptr = keys.data_ptr()
+    dm.apply_online_delta({(20, 21): 4, (3, 4): 1})
+    assert dm.table[0].data_ptr() == keys_ptr
+    host.keys[:] = dm.table[0].numpy().view(np.uint64)
+    host.prior[:] = dm.table[1].numpy()
+    host.online[:] = dm.table[2].numpy()
+    assert host.frequency(20, 21) == 4 and host.frequency(3, 4) == 5 + 1 + 1
+    assert mem.online_counts() == {(3, 4): 3, (10, 11): 2, (20, 21): 4}
+    assert DeviceRecoveryMemory(mem, "cpu", capacity=64, stop_ids=set()).stop_ids is None
