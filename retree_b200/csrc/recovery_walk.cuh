@@ -205,6 +205,9 @@ RT_HD void recovery_walk(const WalkArgs& a) {
     int hit = -1;
     for (int j = 0; j < nc && hit < 0; ++j)
       if (a.child_tok[j] == nxt) hit = j;
+    // every accepted node lies one level below the previous one, so a tree of
+    // n nodes accepts at most n; a parent array with a cycle stops here
+    if (len >= a.n) break;
     if (hit >= 0) {  // exact accept
       cur = a.child_node[hit];
       a.accepted[len++] = cur;

@@ -297,20 +297,27 @@ def allocate_tree_buffers(tree_budget: int, device):
 @torch.inference_mode()
 def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, max_new_tokens: int,
                     block_size: int, stop_token_ids, temperature: float = 0.0, tree_budget: int | None = None,
-                    save_tree_traces: bool = False, draft_fn=None) -> SimpleNamespace:
+                    save_tree_traces: bool = False, draft_fn=None, fused: bool | None = None,
+                    fused_draft: bool = False) -> SimpleNamespace:
     """The DDTree decode loop of ddtree.py:734-968 on the device kernels.
 
     ``target`` is a causal LM whose attention backend is ``"retree_tree"``.
-    ``model`` is the block draft model, called as in ddtree.py:832-844; a
-    ``draft_fn(output_ids, start, round) -> [block_size-1, vocab]`` logits
-    callable may replace it (the draft model is not part of this package).
+    ``model`` is the block draft model (a DFlash module), called as in
+    ddtree.py:832-844 on the target's layer outputs ``model.target_layer_ids``
+    (ddtree.py:811-812, :917-918); a ``draft_fn(output_ids, start, round) ->
+    [block_size-1, vocab]`` logits callable may replace it.  ``fused`` picks
+    the verify forward (None: the fused stages when the model allows them and
+    no hidden states are needed), ``fused_draft`` runs the draft module on the
+    fused stages (``retree_b200.draft.FusedDraft``).
     """
     from .verify import TreeVerifier
 
     if block_size <= 1:
         raise NotImplementedError("block_size <= 1 is the linear DFlash baseline, outside the tree path")
+    layer_ids = None if (model is None or draft_fn is not None) else list(model.target_layer_ids)
     verifier = TreeVerifier(target, tree_budget=(block_size - 1) if tree_budget is None else max(tree_budget, 0),
                             max_length=input_ids.shape[1] + max_new_tokens + 2 * block_size + 8,
-                            draft_horizon=block_size - 1, temperature=temperature)
+                            draft_horizon=block_size - 1, temperature=temperature, target_layer_ids=layer_ids,
+                            fused=fused, fused_draft=fused_draft)
     return verifier.generate(input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
                              draft_model=model, draft_fn=draft_fn, save_tree_traces=save_tree_traces)

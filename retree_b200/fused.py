@@ -70,6 +70,25 @@ def supports(model) -> bool:
     return next(model.parameters()).dtype == torch.bfloat16
 
 
+def rope_tables(rot, device, max_positions: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 ``cos, sin [max_positions, head_dim]``: a rotary module's outputs for positions ``[0, max_positions)``.
+
+    The HF rotary modules compute each position's angles independently
+    (fp32 outer product, then cos/sin cast to the activations' dtype), so the
+    table rows equal what a forward at those positions computes.
+    """
+    cos_parts, sin_parts = [], []
+    dummy = torch.empty((1, 1), dtype=torch.bfloat16, device=device)
+    step = 8192
+    with torch.no_grad():
+        for p0 in range(0, max_positions, step):
+            pos = torch.arange(p0, min(max_positions, p0 + step), device=device).unsqueeze(0)
+            c, s = rot(dummy, pos)
+            cos_parts.append(c[0])
+            sin_parts.append(s[0])
+    return torch.cat(cos_parts).contiguous(), torch.cat(sin_parts).contiguous()
+
+
 def _pack(linears) -> tuple[torch.Tensor, torch.Tensor | None]:
     """One weight (and bias) for several nn.Linear; the modules keep row-block views of it."""
     w = torch.cat([lin.weight.detach() for lin in linears], dim=0).contiguous()
@@ -92,7 +111,8 @@ class _Layer:
 
 
 class FusedTarget:
-    def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto"):
+    def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto",
+                 capture_layers=None):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -151,6 +171,14 @@ class FusedTarget:
         self.act = torch.empty((n, self.inter), **e)
         self.mlp_out = torch.empty((n, self.hidden), **e)
         self.logits = torch.empty((n, self.vocab), **e)
+        # layer outputs the caller wants (HF hidden_states[i + 1] for i in capture_layers),
+        # side by side in one [n, len * hidden] buffer (model/utils.py:40-49)
+        self.capture_layers = None if capture_layers is None else [int(i) for i in capture_layers]
+        self.hidden_out = None
+        if self.capture_layers is not None:
+            if not self.capture_layers or any(i < 0 or i >= len(self.layers) for i in self.capture_layers):
+                raise ValueError(f"capture_layers must name layers in [0, {len(self.layers)})")
+            self.hidden_out = torch.empty((n, len(self.capture_layers) * self.hidden), **e)
         if gemm not in ("auto", "tcgen05", "cublas"):
             raise ValueError("gemm must be 'auto', 'tcgen05' or 'cublas'")
         self.gemm = gemm
@@ -166,18 +194,7 @@ class FusedTarget:
 
     @staticmethod
     def _rope_tables(model, max_positions: int):
-        rot = model.model.rotary_emb
-        dev = next(model.parameters()).device
-        cos_parts, sin_parts = [], []
-        dummy = torch.empty((1, 1), dtype=torch.bfloat16, device=dev)
-        step = 8192
-        with torch.no_grad():
-            for p0 in range(0, max_positions, step):
-                pos = torch.arange(p0, min(max_positions, p0 + step), device=dev).unsqueeze(0)
-                c, s = rot(dummy, pos)
-                cos_parts.append(c[0])
-                sin_parts.append(s[0])
-        return torch.cat(cos_parts).contiguous(), torch.cat(sin_parts).contiguous()
+        return rope_tables(model.model.rotary_emb, next(model.parameters()).device, max_positions)
 
     def _splits(self, n: int) -> int:
         return kernels.default_splits(n, self.hq, self.hkv, self.cache.capacity - n)
@@ -300,6 +317,10 @@ class FusedTarget:
         n = ids.numel()
         if n > self.n_max:
             raise RuntimeError(f"{n} nodes exceed the fused forward's n_max {self.n_max}")
+        last = len(self.layers) - 1
+        # after the residual add that opens layer i + 1, the residual holds layer i's output
+        capture = {} if self.capture_layers is None else {li: j for j, li in enumerate(self.capture_layers)}
+        hid = self.hidden
         ids = ids.reshape(n)
         positions = positions.reshape(n)
         slab = self.cache.slab
@@ -311,6 +332,9 @@ class FusedTarget:
                 kernels.embed_rmsnorm(ids, self.embed, L.in_norm, L.eps_in, res, xn)
             else:
                 kernels.add_rmsnorm(self.mlp_out[:n], res, L.in_norm, L.eps_in, xn)
+                j = capture.get(L.index - 1)
+                if j is not None:
+                    self.hidden_out[:n, j * hid: (j + 1) * hid].copy_(res)
             self._qkv(L, xn, positions, offset, offset_dev)
             kc, vc = slab[2 * L.index], slab[2 * L.index + 1]
             if offset_dev is not None:
@@ -328,4 +352,8 @@ class FusedTarget:
             self._linear(xn, L.gate_up_w, None, self.act[:n], epilogue=1, kind="gate_up")
             self._linear(self.act[:n], L.down_w, None, self.mlp_out[:n], kind="down")
         kernels.add_rmsnorm(self.mlp_out[:n], res, self.final_norm, self.eps, xn)
+        j = capture.get(last)
+        if j is not None:
+            # HF's last hidden state is the final norm's output (utils/output_capturing.py:253-258)
+            self.hidden_out[:n, j * hid: (j + 1) * hid].copy_(xn)
         return self._linear(xn, self.lm_head, None, self.logits[:n], kind="lm_head")

@@ -88,12 +88,14 @@ def retree_generate(model, target, input_ids, mask_token_id, max_new_tokens, blo
                     temperature: float = 0.0, tree_budget: int | None = None,
                     recovery_memory: RecoveryMemory | None = None, gate_threshold: float = 0.01,
                     recovery_online_update: bool = True, recovery_record_top_k: int = 8,
-                    recovery_rescue_top_k: int = 8, draft_fn=None, device_recovery: bool = False):
+                    recovery_rescue_top_k: int = 8, draft_fn=None, device_recovery: bool = False,
+                    fused: bool | None = None, fused_draft: bool = False):
     """ReTree decode loop (retree.py:193-444); ``total_rescued`` counts sibling rescues.
 
     ``device_recovery`` runs the recovery walk on the GPU (rt_recovery_walk)
     over a device copy of ``recovery_memory``; its online counts are applied to
-    ``recovery_memory`` when the request ends.
+    ``recovery_memory`` when the request ends.  ``fused`` / ``fused_draft`` as
+    in ``ddtree_generate``.
     """
     from .verify import TreeVerifier
 
@@ -112,7 +114,9 @@ def retree_generate(model, target, input_ids, mask_token_id, max_new_tokens, blo
 
     verifier = TreeVerifier(target, tree_budget=(block_size - 1) if tree_budget is None else max(tree_budget, 0),
                             max_length=input_ids.shape[1] + max_new_tokens + 2 * block_size + 8,
-                            draft_horizon=block_size - 1, temperature=temperature)
+                            draft_horizon=block_size - 1, temperature=temperature,
+                            target_layer_ids=None if (model is None or draft_fn is not None)
+                            else list(model.target_layer_ids), fused=fused, fused_draft=fused_draft)
     if device_recovery and recovery_memory is not None:
         from .recovery_device import DeviceRecoveryMemory
         dm = DeviceRecoveryMemory(recovery_memory, verifier.device, stop_ids=stop_set)

@@ -57,7 +57,7 @@ def extract_context_feature(hidden_states, layer_ids):
 class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
                  temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None,
-                 gemm: str = "auto"):
+                 gemm: str = "auto", fused_draft: bool = False):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -108,15 +108,20 @@ class TreeVerifier:
         self.debug = False  # keep the posterior and the pre-compaction cache of the last round
         self.strategy, self.params = resolve_strategy()
         # verify forward: fused stages (retree_b200.fused) unless the model is not
-        # one they cover or the caller needs the HF hidden states
+        # one they cover; with target_layer_ids the fused forward also writes the
+        # selected layer outputs (the draft's context features)
         if fused is None:
             # (a target split by KV head keeps the module forward: the fused stages
             # with per-layer all-gathers have not been timed on several GPUs yet)
             fused = (target_layer_ids is None and fused_mod.supports(target)
                      and not hasattr(target, "_rt_local_kv_heads"))
-        if fused and target_layer_ids is not None:
-            raise RuntimeError("the fused verify forward does not return hidden states")
-        self.fused = fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm) if fused else None
+        self.fused = (fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm,
+                                            capture_layers=target_layer_ids) if fused else None)
+        # draft forward: the DFlash module (reference layout) on the fused stages
+        # (retree_b200.draft.FusedDraft) when asked for and supported
+        self.fused_draft = bool(fused_draft)
+        self._draft_runner = None
+        self._draft_cache = None
 
     # ------------------------------------------------------------------ prefill
     @torch.inference_mode()
@@ -138,6 +143,10 @@ class TreeVerifier:
         self.start_dev.fill_(n)
         self.graph = None
         self.cache.use_device_length(device_mode)
+        # a new request: the draft's cache starts empty
+        self._draft_cache = None
+        if self._draft_runner is not None:
+            self._draft_runner.reset()
 
     @torch.inference_mode()
     def prefill_random(self, length: int, seed: int = 0, vocab: int | None = None) -> None:
@@ -174,6 +183,8 @@ class TreeVerifier:
         pre-commit start from ``start_dev[1]``: no host value of the round
         changes between rounds, so one capture serves every prefix length.
         """
+        if enabled and self.target_layer_ids is not None and self.fused is None:
+            raise RuntimeError("graph mode with target_layer_ids needs the fused verify forward")
         self.graph_mode = bool(enabled)
         self.graph = None
         self.cache.use_device_length(self.graph_mode)
@@ -253,6 +264,8 @@ class TreeVerifier:
             self.graph.replay()
             kernels._count(self.launches_per_round)
             acc = int(self.walk["accepted_len"].item())
+        if self.target_layer_ids is not None:
+            self.target_hidden = self.fused.hidden_out.index_select(0, self.walk["accepted"][:acc]).unsqueeze(0)
         self.start += acc
         for layer in self.cache.layers:
             layer.length = self.start
@@ -327,8 +340,11 @@ class TreeVerifier:
             layer.length = start + acc_len
         if self.target_layer_ids is not None:
             keep_idx = self.walk["accepted"][:acc_len] if accepted is None else keep
-            self.target_hidden = extract_context_feature(out.hidden_states, self.target_layer_ids).index_select(
-                1, keep_idx)
+            if self.fused is not None:
+                self.target_hidden = self.fused.hidden_out[:n].index_select(0, keep_idx).unsqueeze(0)
+            else:
+                self.target_hidden = extract_context_feature(out.hidden_states, self.target_layer_ids).index_select(
+                    1, keep_idx)
         self.start = start + acc_len
         self._tick("commit", t)
         return acc_len
@@ -338,10 +354,19 @@ class TreeVerifier:
         start = self.start
         if draft_fn is not None:
             return draft_fn(self.output_ids, start, round_idx)
+        if self.target_hidden is None:
+            raise RuntimeError("the draft model needs the target's hidden states: pass target_layer_ids")
+        if self.fused_draft:
+            if self._draft_runner is None:
+                from .draft import FusedDraft
+                self._draft_runner = FusedDraft(draft_model, self.target, capacity=self.max_length + block_size + 8,
+                                                block_size=block_size)
+            return self._draft_runner.forward(self.output_ids[start: start + block_size], self.target_hidden, start,
+                                              horizon=block_size - 1)
         # the reference's draft call (ddtree.py:828-845)
         block = self.output_ids[start: start + block_size].clone().unsqueeze(0)
         noise = self.target.model.embed_tokens(block)
-        if not hasattr(self, "_draft_cache"):
+        if self._draft_cache is None:
             from transformers import DynamicCache
             self._draft_cache = DynamicCache()
             self._positions = torch.arange(self.output_ids.numel(), device=self.device).unsqueeze(0)
