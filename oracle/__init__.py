@@ -18,4 +18,7 @@ Modules:
              (transformers/integrations/sdpa_attention.py)
   recovery   recovery memory and the target-gated sibling-recovery walk
              (model/recovery.py, retree.py)
+  dflash     the DFlash block-draft forward with its cache crop
+             (model/dflash.py), golden outputs from the reference module
+             (tests/golden/make_dflash_golden.py)
 """
