@@ -94,3 +94,25 @@ def test_recovery_walk_matches_reference():
             disallow_rescue_target_ids=None if c["stop"] is None else set(c["stop"]))
         assert (acc, nxt, resc) == (c["accepted"], c["next"], c["rescued"]), i
         assert sorted([d, tt, n] for (d, tt), n in mem.online_counts().items()) == c["online"]
+
+
+def test_files_match_the_reference_writer_byte_for_byte(golden_dir):
+    """save_prior / save_runtime_state write what the reference's RecoveryMemory wrote for the same records,
+    and loading those files gives back the same tables (tests/golden/make_recovery_files.py)."""
+    import importlib.util
+    import tempfile
+
+    spec = importlib.util.spec_from_file_location("make_recovery_files", f"{golden_dir}/make_recovery_files.py")
+    gen = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(gen)
+    mem = RecoveryMemory(freq_threshold=4)
+    for kind, d, t, c in gen.records():
+        (mem.record_prior if kind == "prior" else mem.record_online)(d, t, c)
+    with tempfile.TemporaryDirectory() as td:
+        for name, save in (("recovery_prior.json", mem.save_prior), ("recovery_state.json", mem.save_runtime_state)):
+            save(str(Path(td) / name))
+            assert (Path(td) / name).read_bytes() == (Path(golden_dir) / name).read_bytes(), name
+    loaded = RecoveryMemory.from_file(f"{golden_dir}/recovery_state.json", freq_threshold=4, load_online=True)
+    assert loaded.prior_counts() == mem.prior_counts() and loaded.online_counts() == mem.online_counts()
+    flat = RecoveryMemory.from_file(f"{golden_dir}/recovery_prior.json")
+    assert flat.prior_counts() == mem.prior_counts() and flat.online_counts() == {}
