@@ -139,6 +139,29 @@ int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, con
                  int head_dim, float scale, int num_splits, int path, void* workspace, size_t workspace_bytes,
                  int* status, rt_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Tree-verify attention that also warms the L2 with up to two ranges of
+ * device memory -- the weights of the projections that follow it.
+ * No counterpart in the reference: at tree sizes this attention is bound by
+ * latency, not HBM bandwidth, so while it runs the HBM has room to move the
+ * next projections' weights into the 126 MB L2 (cp.async.bulk.prefetch.L2
+ * requests spread over the launch's CTAs, issued by the producer warp's idle
+ * lanes; nothing waits for them).  Same arguments and results as
+ * rt_tree_attn.  A range with ptr NULL or bytes <= 0 is skipped; ptr must be
+ * 16-byte aligned and bytes is rounded down to a multiple of 16.  Only the
+ * tcgen05 path (n * group >= 64, or path 1) issues the requests.
+ * ---------------------------------------------------------------------- */
+typedef struct rt_l2_prefetch {
+  const void* ptr[2];
+  int64_t bytes[2];
+} rt_l2_prefetch;
+int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
+                    int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
+                    int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words, int n,
+                    int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads, int num_kv_heads,
+                    int head_dim, float scale, int num_splits, int path, void* workspace, size_t workspace_bytes,
+                    const rt_l2_prefetch* prefetch, int* status, rt_stream_t stream);
+
 /* Number of key splits rt_tree_attn chooses for this shape (num_splits = 0). */
 int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len);
 

@@ -32,6 +32,8 @@ SIGNATURES = {
     "rt_tree_attn_workspace_size": (_SZ, [_I, _I, _I, _I, _I64, _I]),
     "rt_tree_attn": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                           _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P]),
+    "rt_tree_attn_ex": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
+                             _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P, _P]),
     "rt_tree_attn_default_splits": (_I, [_I, _I, _I, _I64]),
     "rt_tree_attn_noalloc_max_bytes": (_SZ, []),
     "rt_tree_attn_noalloc": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
@@ -57,6 +59,12 @@ SIGNATURES = {
 RT_EPI_STORE = 0
 RT_EPI_SILU_MUL = 1
 RT_EPI_QKV_ROPE = 2
+
+
+class L2Prefetch(ctypes.Structure):
+    """``rt_l2_prefetch`` (include/retree_b200.h): up to two device ranges to warm in L2."""
+
+    _fields_ = [("ptr", _P * 2), ("bytes", ctypes.c_int64 * 2)]
 
 
 class QkvEpilogue(ctypes.Structure):

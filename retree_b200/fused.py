@@ -38,6 +38,8 @@ like the library GEMM, in their own summation order.
 
 from __future__ import annotations
 
+import os
+
 import torch
 from torch import nn
 
@@ -112,7 +114,7 @@ class _Layer:
 
 class FusedTarget:
     def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto",
-                 capture_layers=None):
+                 capture_layers=None, attn_l2_prefetch: int | None = None):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -179,6 +181,19 @@ class FusedTarget:
             if not self.capture_layers or any(i < 0 or i >= len(self.layers) for i in self.capture_layers):
                 raise ValueError(f"capture_layers must name layers in [0, {len(self.layers)})")
             self.hidden_out = torch.empty((n, len(self.capture_layers) * self.hidden), **e)
+        # L2 warm-up from inside each layer's attention launch: up to this many
+        # bytes of the projections that follow it (o_proj, then the head of
+        # gate|up); the attention is latency-bound and leaves the HBM idle
+        if attn_l2_prefetch is None:
+            attn_l2_prefetch = int(float(os.environ.get("RETREE_B200_ATTN_L2PF_MB", "0")) * (1 << 20))
+        self.attn_l2_prefetch = max(0, int(attn_l2_prefetch))
+        for L in self.layers:
+            L.l2pf = None
+            if self.attn_l2_prefetch > 0:
+                o_bytes = L.o_w.numel() * L.o_w.element_size()
+                first = min(o_bytes, self.attn_l2_prefetch)
+                rest = self.attn_l2_prefetch - first
+                L.l2pf = [(L.o_w, first)] + ([(L.gate_up_w, rest)] if rest > 0 else [])
         if gemm not in ("auto", "tcgen05", "cublas"):
             raise ValueError("gemm must be 'auto', 'tcgen05' or 'cublas'")
         self.gemm = gemm
@@ -339,10 +354,12 @@ class FusedTarget:
             kc, vc = slab[2 * L.index], slab[2 * L.index + 1]
             if offset_dev is not None:
                 kernels.tree_attention(self.q[:n], kc, vc, bits, cap - n, scale=L.scale, out=self.attn[:n],
-                                       num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap)
+                                       num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap,
+                                       l2_prefetch=L.l2pf)
             else:
                 kernels.tree_attention(self.q[:n], kc[:, : offset + n], vc[:, : offset + n], bits, offset,
-                                       scale=L.scale, out=self.attn[:n], num_splits=splits, kv_capacity=cap)
+                                       scale=L.scale, out=self.attn[:n], num_splits=splits, kv_capacity=cap,
+                                       l2_prefetch=L.l2pf)
             attn = self.attn[:n]
             if L.split is not None:
                 group, world, _ = L.split

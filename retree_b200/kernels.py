@@ -180,12 +180,15 @@ def _as3(t: torch.Tensor) -> torch.Tensor:
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits: torch.Tensor, prefix_len: int,
                    scale: float | None = None, out: torch.Tensor | None = None, num_splits: int = 0,
                    path: int = 0, prefix_len_dev: torch.Tensor | None = None,
-                   kv_capacity: int | None = None) -> torch.Tensor:
+                   kv_capacity: int | None = None, l2_prefetch=None) -> torch.Tensor:
     """Masked GQA attention of n tree nodes over ``[prefix ; tree block]``.
 
     q: ``[n, Hq, D]`` or HF's ``[1, Hq, n, D]``; k, v: ``[Hkv, S, D]`` or
     ``[1, Hkv, S, D]`` (rows ``[0, prefix_len + n)`` are used);
     mask_bits: int32 ``[n, W]`` ancestor bits of the tree block.
+    ``l2_prefetch``: up to two ``(tensor, nbytes)`` ranges (device memory the
+    next kernels read, e.g. their weights) that the launch asks the L2 to load
+    while it runs (rt_tree_attn_ex); results do not depend on it.
     Returns ``out`` ``[n, Hq, D]`` bf16 (HF's ``[1, n, Hq, D]`` after unsqueeze).
     """
     lib = _lib.load()
@@ -213,11 +216,23 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
     splits = num_splits if num_splits > 0 else lib.rt_tree_attn_default_splits(n, hq, hkv, int(prefix_len))
     ws_bytes = lib.rt_tree_attn_workspace_size(n, hq, hkv, d, int(prefix_len), splits)
     ws = _STATE.buffer(q.device, "attn_ws", ws_bytes) if ws_bytes else None
-    rc = lib.rt_tree_attn(q.data_ptr(), q.stride(0) * es, q.stride(1) * es, k.data_ptr(), v.data_ptr(),
-                          k.stride(0) * es, k.stride(1) * es, cap, out.data_ptr(), out.stride(0) * es,
-                          out.stride(1) * es, mask_bits.data_ptr(), words, n, int(prefix_len), _ptr(prefix_len_dev),
-                          hq, hkv, d, scale, splits, path, _ptr(ws), ws_bytes,
-                          _STATE.status(q.device).data_ptr(), _stream(q.device))
+    pf = None
+    if l2_prefetch:
+        if len(l2_prefetch) > 2:
+            raise ValueError("at most two L2 prefetch ranges")
+        pf = _lib.L2Prefetch()
+        for i, (t, nbytes) in enumerate(l2_prefetch):
+            _require_cuda(t)
+            if not t.is_contiguous():
+                raise RuntimeError("an L2 prefetch range must be a contiguous tensor")
+            pf.ptr[i] = t.data_ptr()
+            pf.bytes[i] = max(0, min(int(nbytes), t.numel() * t.element_size()))
+    rc = lib.rt_tree_attn_ex(q.data_ptr(), q.stride(0) * es, q.stride(1) * es, k.data_ptr(), v.data_ptr(),
+                             k.stride(0) * es, k.stride(1) * es, cap, out.data_ptr(), out.stride(0) * es,
+                             out.stride(1) * es, mask_bits.data_ptr(), words, n, int(prefix_len),
+                             _ptr(prefix_len_dev), hq, hkv, d, scale, splits, path, _ptr(ws), ws_bytes,
+                             None if pf is None else ctypes.addressof(pf), _STATE.status(q.device).data_ptr(),
+                             _stream(q.device))
     _lib.check(rc, "rt_tree_attn")
     _count(2 if splits > 1 else 1)
     return out

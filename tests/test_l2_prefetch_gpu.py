@@ -1,0 +1,59 @@
+"""The attention launch's L2 warm-up (rt_tree_attn_ex) changes no result.
+
+The requests only load lines into L2, so the attention output and the fused
+verify forward's logits must be bit-identical with and without them, for
+ranges that are shorter than, equal to, and longer than the CTAs' shares.
+"""
+
+import pytest
+import torch
+
+from retree_b200 import fused, kernels
+from retree_b200.cache import TreeKVCache
+from retree_b200.target import build_target, qwen3_config
+from tests.gpu_util import bits_tensor, cuda, random_tree
+
+pytestmark = [pytest.mark.gpu, pytest.mark.late]
+
+
+@torch.inference_mode()
+@pytest.mark.parametrize("n,prefix", [(17, 2048), (65, 700), (257, 4096)])
+def test_attention_output_is_unchanged_by_l2_warm_up(n, prefix):
+    dev = cuda()
+    g = torch.Generator(device=dev).manual_seed(n)
+    cap = prefix + n + 64
+    k = torch.randn((8, cap, 128), device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn((8, cap, 128), device=dev, generator=g).to(torch.bfloat16)
+    q = torch.randn((n, 32, 128), device=dev, generator=g).to(torch.bfloat16)
+    _, vis = random_tree(n, n - 1)
+    assert vis.shape == (n, n)
+    bits = bits_tensor(vis, dev)
+    want = kernels.tree_attention(q, k, v, bits, prefix, kv_capacity=cap).clone()
+    w1 = torch.randn((4096, 2560), device=dev, generator=g).to(torch.bfloat16)
+    w2 = torch.randn((1000, 24), device=dev, generator=g).to(torch.bfloat16)
+    for ranges in ([(w1, w1.numel() * 2)], [(w1, 5 << 20), (w2, w2.numel() * 2)], [(w2, 100)]):
+        got = kernels.tree_attention(q, k, v, bits, prefix, kv_capacity=cap, l2_prefetch=ranges)
+        torch.cuda.synchronize()
+        kernels.check_device_status(dev)
+        assert torch.equal(got, want)
+
+
+@torch.inference_mode()
+def test_fused_forward_is_unchanged_by_l2_warm_up():
+    dev = cuda()
+    cfg = qwen3_config("small", hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
+                       num_key_value_heads=2, vocab_size=2000, tie_word_embeddings=False)
+    model = build_target(cfg, device=dev, seed=2)
+    L, n = 300, 17
+    outs = []
+    for pf in (0, 1 << 20, 64 << 20):
+        cache = TreeKVCache.for_model(model.config, capacity=512, device=dev)
+        cache.slab.copy_(torch.randn(cache.slab.shape, device=dev,
+                                     generator=torch.Generator(device=dev).manual_seed(1)).to(torch.bfloat16))
+        ft = fused.FusedTarget(model, cache, n_max=32, gemm="cublas", attn_l2_prefetch=pf)
+        tok = torch.randint(0, 2000, (n,), device=dev, generator=torch.Generator(device=dev).manual_seed(3))
+        pos = torch.arange(L, L + n, device=dev)
+        bits = bits_tensor(random_tree(4, n - 1)[1], dev)
+        outs.append(ft.forward(tok, pos, bits, offset=L).clone())
+    kernels.check_device_status(dev)
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
