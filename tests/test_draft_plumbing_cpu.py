@@ -68,7 +68,7 @@ def fake_kernels(monkeypatch):
         return q_out
 
     def tree_attention(q, k, v, bits, prefix_len, scale=None, out=None, num_splits=0, path=0, prefix_len_dev=None,
-                       kv_capacity=None):
+                       kv_capacity=None, l2_prefetch=None):
         n, hq, d = q.shape
         L = int(prefix_len) + (0 if prefix_len_dev is None else int(prefix_len_dev[0]))
         hkv = k.shape[0]
