@@ -80,6 +80,8 @@ def parse():
                     help="run the verify forward through the transformers modules instead of the fused stages")
     ap.add_argument("--attn-l2-prefetch", type=float, default=0.0, metavar="MB",
                     help="MB of the following projections' weights each attention launch warms in L2")
+    ap.add_argument("--l2-stream", action="store_true",
+                    help="warm the next projection's weights in L2 from a side stream next to each launch")
     return ap.parse_args()
 
 
@@ -282,7 +284,7 @@ def run_ours(args, wl, rank, world, local_rank):
     def fresh():
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
                          fused=not args.hf_forward, gemm=args.gemm,
-                         attn_l2_prefetch=int(args.attn_l2_prefetch * 2**20))
+                         attn_l2_prefetch=int(args.attn_l2_prefetch * 2**20), l2_stream=args.l2_stream)
         if wl.get("split"):
             v.prefill_random(plen, seed=req)
         else:
@@ -451,7 +453,7 @@ def run_ours(args, wl, rank, world, local_rank):
                    "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
                    "projections": projections,
-                   "attn_l2_prefetch_mb": args.attn_l2_prefetch,
+                   "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer)"
                                    if wl.get("split") else f"dp{world} (one request per GPU)" + (
                                        ", recovery-delta all-gather per step" if world > 1 else "")),

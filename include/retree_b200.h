@@ -140,27 +140,36 @@ int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, con
                  int* status, rt_stream_t stream);
 
 /* ------------------------------------------------------------------------
- * Tree-verify attention that also warms the L2 with up to two ranges of
- * device memory -- the weights of the projections that follow it.
- * No counterpart in the reference: at tree sizes this attention is bound by
- * latency, not HBM bandwidth, so while it runs the HBM has room to move the
- * next projections' weights into the 126 MB L2 (cp.async.bulk.prefetch.L2
- * requests spread over the launch's CTAs, issued by the producer warp's idle
- * lanes; nothing waits for them).  Same arguments and results as
- * rt_tree_attn.  A range with ptr NULL or bytes <= 0 is skipped; ptr must be
- * 16-byte aligned and bytes is rounded down to a multiple of 16.  Only the
- * tcgen05 path (n * group >= 64, or path 1) issues the requests.
+ * L2 warm-up.
+ * No counterpart in the reference.  At tree sizes the verify forward's
+ * kernels are bound by latency, not by HBM bandwidth, so while one runs the
+ * HBM has room to move the weights the next one reads into the 126 MB L2.
+ * A warm-up asks the L2 to load up to RT_L2_MAX_RANGES ranges of device
+ * memory with cp.async.bulk.prefetch.L2 requests (32 KB each); nothing waits
+ * for them and no result depends on them.  A range with ptr NULL or
+ * bytes <= 0 is skipped; ptr must be 16-byte aligned and bytes is rounded
+ * down to a multiple of 16; count is 0..RT_L2_MAX_RANGES.
+ *
+ * rt_l2_prefetch: a kernel of `ctas` one-warp CTAs (1..1024) that issues the
+ *   requests (launched on a side stream next to a kernel, it warms what the
+ *   following kernel reads).
+ * rt_tree_attn_ex: rt_tree_attn whose tcgen05-path CTAs also issue requests
+ *   for their share of `prefetch` from the producer warp's idle lanes; same
+ *   arguments and results as rt_tree_attn otherwise (prefetch may be NULL).
  * ---------------------------------------------------------------------- */
-typedef struct rt_l2_prefetch {
-  const void* ptr[2];
-  int64_t bytes[2];
-} rt_l2_prefetch;
+#define RT_L2_MAX_RANGES 16
+typedef struct rt_l2_ranges {
+  int count;
+  const void* ptr[RT_L2_MAX_RANGES];
+  int64_t bytes[RT_L2_MAX_RANGES];
+} rt_l2_ranges;
+int rt_l2_prefetch(const rt_l2_ranges* ranges, int ctas, rt_stream_t stream);
 int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
                     int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
                     int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words, int n,
                     int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads, int num_kv_heads,
                     int head_dim, float scale, int num_splits, int path, void* workspace, size_t workspace_bytes,
-                    const rt_l2_prefetch* prefetch, int* status, rt_stream_t stream);
+                    const rt_l2_ranges* prefetch, int* status, rt_stream_t stream);
 
 /* Number of key splits rt_tree_attn chooses for this shape (num_splits = 0). */
 int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len);

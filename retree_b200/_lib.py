@@ -35,6 +35,7 @@ SIGNATURES = {
     "rt_tree_attn_ex": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                              _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P, _P]),
     "rt_tree_attn_default_splits": (_I, [_I, _I, _I, _I64]),
+    "rt_l2_prefetch": (_I, [_P, _I, _P]),
     "rt_tree_attn_noalloc_max_bytes": (_SZ, []),
     "rt_tree_attn_noalloc": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                                   _I, _I, _I, _F, _I, _I, _P, _P]),
@@ -61,10 +62,13 @@ RT_EPI_SILU_MUL = 1
 RT_EPI_QKV_ROPE = 2
 
 
-class L2Prefetch(ctypes.Structure):
-    """``rt_l2_prefetch`` (include/retree_b200.h): up to two device ranges to warm in L2."""
+RT_L2_MAX_RANGES = 16
 
-    _fields_ = [("ptr", _P * 2), ("bytes", ctypes.c_int64 * 2)]
+
+class L2Ranges(ctypes.Structure):
+    """``rt_l2_ranges`` (include/retree_b200.h): device ranges to warm in L2."""
+
+    _fields_ = [("count", ctypes.c_int), ("ptr", _P * RT_L2_MAX_RANGES), ("bytes", ctypes.c_int64 * RT_L2_MAX_RANGES)]
 
 
 class QkvEpilogue(ctypes.Structure):

@@ -72,9 +72,7 @@ struct AttnParams {
   const char* k;
   const char* v;
   int64_t kv_head_stride, kv_row_stride;
-  // L2 warm-up ranges (rt_tree_attn_ex): 16-byte aligned, bytes a multiple of 16
-  const char* pf_ptr[2];
-  int64_t pf_bytes[2];
+  L2Ranges pf;  // L2 warm-up (rt_tree_attn_ex)
 };
 
 struct Barriers {
@@ -136,25 +134,6 @@ __device__ __forceinline__ uint32_t visible_word(int64_t k0, int64_t L, int n, c
   const int64_t lim = static_cast<int64_t>(n) - t0;  // columns c < lim have t < n
   if (lim < 32) tb &= lim <= 0 ? 0u : ((1u << lim) - 1u);
   return bits | tb;
-}
-
-// This CTA's share of the L2 warm-up ranges, in 32 KB requests spread over
-// `parts` lanes (lane `part`): CTA c of C takes bytes [c*per, (c+1)*per).
-__device__ __forceinline__ void l2_warm_share(const AttnParams& p, int part, int parts) {
-  const int64_t ctas = static_cast<int64_t>(gridDim.x) * gridDim.y * gridDim.z;
-  const int64_t c = blockIdx.x + static_cast<int64_t>(gridDim.x) * (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
-  constexpr int64_t kPiece = 32768;
-  for (int r = 0; r < 2; ++r) {
-    const int64_t bytes = p.pf_bytes[r];
-    if (p.pf_ptr[r] == nullptr || bytes <= 0) continue;
-    const int64_t per = (((bytes + ctas - 1) / ctas) + 15) & ~static_cast<int64_t>(15);
-    const int64_t b0 = c * per, b1 = min(bytes, b0 + per);
-    for (int64_t o = b0 + static_cast<int64_t>(part) * kPiece; o < b1; o += static_cast<int64_t>(parts) * kPiece) {
-      const int64_t len = min(kPiece, b1 - o);
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.pf_ptr[r] + o), "r"(static_cast<uint32_t>(len))
-                   : "memory");
-    }
-  }
 }
 
 __device__ __forceinline__ uint32_t ex2_f16x2(float lo, float hi) {
@@ -308,8 +287,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       pdl_wait();
     } else {
       pdl_wait();
-      // idle lanes: warm the L2 with the following projections' weights
-      l2_warm_share(p, lane - 2, 30);
+      // idle lanes: warm the L2 with what the following kernels read
+      if (p.pf.count > 0) {
+        const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) * (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
+        l2_warm_share(p.pf, cta, static_cast<int64_t>(gridDim.x) * gridDim.y * gridDim.z, lane - 2, 30);
+      }
     }
   } else if (warp == kMmaWarp) {
     pdl_wait();
@@ -801,7 +783,7 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
                                void* out, int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask,
                                int mask_words, int n, int64_t prefix_len, const int64_t* prefix_len_dev,
                                int num_q_heads, int num_kv_heads, int head_dim, float scale, int num_splits, int path,
-                               void* workspace, size_t workspace_bytes, const rt_l2_prefetch* prefetch, int* status,
+                               void* workspace, size_t workspace_bytes, const rt_l2_ranges* prefetch, int* status,
                                rt_stream_t stream) {
   if (!q || !k || !v || !out || !mask) return RT_ERR_INVALID_ARGUMENT;
   if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || prefix_len < 0)
@@ -843,14 +825,7 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
   p.v = static_cast<const char*>(v);
   p.kv_head_stride = kv_head_stride;
   p.kv_row_stride = kv_row_stride;
-  if (prefetch != nullptr) {
-    for (int r = 0; r < 2; ++r) {
-      if (prefetch->ptr[r] == nullptr || prefetch->bytes[r] <= 0) continue;
-      if (reinterpret_cast<uintptr_t>(prefetch->ptr[r]) & 15) return RT_ERR_INVALID_ARGUMENT;
-      p.pf_ptr[r] = static_cast<const char*>(prefetch->ptr[r]);
-      p.pf_bytes[r] = prefetch->bytes[r] & ~static_cast<int64_t>(15);
-    }
-  }
+  if (l2_ranges_from(prefetch, &p.pf) != RT_OK) return RT_ERR_INVALID_ARGUMENT;
   if (num_splits > 1) {
     const size_t need = rt_tree_attn_workspace_size(n, num_q_heads, num_kv_heads, head_dim, prefix_len, num_splits);
     if (workspace == nullptr || workspace_bytes < need) return RT_ERR_WORKSPACE;

@@ -114,7 +114,8 @@ class _Layer:
 
 class FusedTarget:
     def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto",
-                 capture_layers=None, attn_l2_prefetch: int | None = None):
+                 capture_layers=None, attn_l2_prefetch: int | None = None, l2_stream: bool | None = None,
+                 l2_stream_budget: int = 64 << 20):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -194,6 +195,28 @@ class FusedTarget:
                 first = min(o_bytes, self.attn_l2_prefetch)
                 rest = self.attn_l2_prefetch - first
                 L.l2pf = [(L.o_w, first)] + ([(L.gate_up_w, rest)] if rest > 0 else [])
+        # L2 warm-up on a side stream: next to each launch, a small rt_l2_prefetch
+        # kernel asks the L2 for the weights of the projection after it (at most
+        # l2_stream_budget bytes each): o_proj next to the QKV projection, gate|up
+        # next to the attention and o_proj, down next to gate|up, the next
+        # layer's q|k|v next to down
+        if l2_stream is None:
+            l2_stream = os.environ.get("RETREE_B200_L2_STREAM", "0") not in ("", "0")
+        self.l2_stream = bool(l2_stream)
+        self.l2_stream_budget = max(0, int(l2_stream_budget))
+        self._side = None
+        if self.l2_stream:
+            nb = lambda t: t.numel() * t.element_size()  # noqa: E731
+            cap = self.l2_stream_budget
+            for i, L in enumerate(self.layers):
+                gu = nb(L.gate_up_w)
+                head = min(gu, cap)
+                nxt = self.layers[i + 1].qkv_w if i + 1 < len(self.layers) else self.lm_head
+                L.warm = {"qkv": [(L.o_w, min(nb(L.o_w), cap))],
+                          "attn": [(L.gate_up_w, head)],
+                          "o": [(L.gate_up_w[head // nb(L.gate_up_w[0]):], min(gu - head, cap))] if gu > head else [],
+                          "gate_up": [(L.down_w, min(nb(L.down_w), cap))],
+                          "down": [(nxt, min(nb(nxt), cap))]}
         if gemm not in ("auto", "tcgen05", "cublas"):
             raise ValueError("gemm must be 'auto', 'tcgen05' or 'cublas'")
         self.gemm = gemm
@@ -319,6 +342,18 @@ class FusedTarget:
         kernels.qk_norm_rope_append(self.qkv[:n], L.hq, L.hkv, L.q_norm, L.k_norm, L.eps_qk, self.cos, self.sin,
                                     positions, self.q[:n], kc, vc, offset=offset, offset_dev=offset_dev)
 
+    def _warm(self, L, kind: str) -> None:
+        """Launch the L2 warm-up planned next to ``kind`` of layer ``L`` on the side stream."""
+        ranges = [(t, b) for t, b in L.warm.get(kind, []) if b > 0]
+        if not ranges:
+            return
+        main = torch.cuda.current_stream(self.device)
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        self._side.wait_stream(main)  # starts when the kernel before this launch is done
+        with torch.cuda.stream(self._side):
+            kernels.l2_prefetch(ranges, ctas=16, device=self.device)
+
     @torch.inference_mode()
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, bits: torch.Tensor, offset: int = 0,
                 offset_dev: torch.Tensor | None = None) -> torch.Tensor:
@@ -342,6 +377,7 @@ class FusedTarget:
         cap = self.cache.capacity
         splits = self._splits(n)
         res, xn = self.residual[:n], self.xnorm[:n]
+        warm = self._warm if self.l2_stream else (lambda L, kind: None)
         for L in self.layers:
             if L.index == 0:
                 kernels.embed_rmsnorm(ids, self.embed, L.in_norm, L.eps_in, res, xn)
@@ -350,8 +386,10 @@ class FusedTarget:
                 j = capture.get(L.index - 1)
                 if j is not None:
                     self.hidden_out[:n, j * hid: (j + 1) * hid].copy_(res)
+            warm(L, "qkv")
             self._qkv(L, xn, positions, offset, offset_dev)
             kc, vc = slab[2 * L.index], slab[2 * L.index + 1]
+            warm(L, "attn")
             if offset_dev is not None:
                 kernels.tree_attention(self.q[:n], kc, vc, bits, cap - n, scale=L.scale, out=self.attn[:n],
                                        num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap,
@@ -364,13 +402,19 @@ class FusedTarget:
             if L.split is not None:
                 group, world, _ = L.split
                 attn = gather_heads(attn.unsqueeze(0), group, world)[0]
+            warm(L, "o")
             self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n], kind="o")
             kernels.add_rmsnorm(self.o[:n], res, L.post_norm, L.eps_post, xn)
+            warm(L, "gate_up")
             self._linear(xn, L.gate_up_w, None, self.act[:n], epilogue=1, kind="gate_up")
+            warm(L, "down")
             self._linear(self.act[:n], L.down_w, None, self.mlp_out[:n], kind="down")
         kernels.add_rmsnorm(self.mlp_out[:n], res, self.final_norm, self.eps, xn)
         j = capture.get(last)
         if j is not None:
             # HF's last hidden state is the final norm's output (utils/output_capturing.py:253-258)
             self.hidden_out[:n, j * hid: (j + 1) * hid].copy_(xn)
-        return self._linear(xn, self.lm_head, None, self.logits[:n], kind="lm_head")
+        logits = self._linear(xn, self.lm_head, None, self.logits[:n], kind="lm_head")
+        if self._side is not None:
+            torch.cuda.current_stream(self.device).wait_stream(self._side)  # rejoin (graph capture needs it)
+        return logits

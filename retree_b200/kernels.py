@@ -186,7 +186,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
     q: ``[n, Hq, D]`` or HF's ``[1, Hq, n, D]``; k, v: ``[Hkv, S, D]`` or
     ``[1, Hkv, S, D]`` (rows ``[0, prefix_len + n)`` are used);
     mask_bits: int32 ``[n, W]`` ancestor bits of the tree block.
-    ``l2_prefetch``: up to two ``(tensor, nbytes)`` ranges (device memory the
+    ``l2_prefetch``: up to 16 ``(tensor, nbytes)`` ranges (device memory the
     next kernels read, e.g. their weights) that the launch asks the L2 to load
     while it runs (rt_tree_attn_ex); results do not depend on it.
     Returns ``out`` ``[n, Hq, D]`` bf16 (HF's ``[1, n, Hq, D]`` after unsqueeze).
@@ -216,17 +216,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
     splits = num_splits if num_splits > 0 else lib.rt_tree_attn_default_splits(n, hq, hkv, int(prefix_len))
     ws_bytes = lib.rt_tree_attn_workspace_size(n, hq, hkv, d, int(prefix_len), splits)
     ws = _STATE.buffer(q.device, "attn_ws", ws_bytes) if ws_bytes else None
-    pf = None
-    if l2_prefetch:
-        if len(l2_prefetch) > 2:
-            raise ValueError("at most two L2 prefetch ranges")
-        pf = _lib.L2Prefetch()
-        for i, (t, nbytes) in enumerate(l2_prefetch):
-            _require_cuda(t)
-            if not t.is_contiguous():
-                raise RuntimeError("an L2 prefetch range must be a contiguous tensor")
-            pf.ptr[i] = t.data_ptr()
-            pf.bytes[i] = max(0, min(int(nbytes), t.numel() * t.element_size()))
+    pf = _l2_ranges(l2_prefetch) if l2_prefetch else None
     rc = lib.rt_tree_attn_ex(q.data_ptr(), q.stride(0) * es, q.stride(1) * es, k.data_ptr(), v.data_ptr(),
                              k.stride(0) * es, k.stride(1) * es, cap, out.data_ptr(), out.stride(0) * es,
                              out.stride(1) * es, mask_bits.data_ptr(), words, n, int(prefix_len),
@@ -236,6 +226,31 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
     _lib.check(rc, "rt_tree_attn")
     _count(2 if splits > 1 else 1)
     return out
+
+
+def _l2_ranges(ranges) -> "_lib.L2Ranges":
+    """``rt_l2_ranges`` from ``(tensor, nbytes)`` pairs: the first ``nbytes`` of each contiguous CUDA tensor."""
+    if len(ranges) > _lib.RT_L2_MAX_RANGES:
+        raise ValueError(f"at most {_lib.RT_L2_MAX_RANGES} L2 ranges")
+    r = _lib.L2Ranges()
+    r.count = len(ranges)
+    for i, (t, nbytes) in enumerate(ranges):
+        _require_cuda(t)
+        if not t.is_contiguous():
+            raise RuntimeError("an L2 range must be a contiguous tensor")
+        r.ptr[i] = t.data_ptr()
+        r.bytes[i] = max(0, min(int(nbytes), t.numel() * t.element_size()))
+    return r
+
+
+def l2_prefetch(ranges, ctas: int = 16, device=None) -> None:
+    """Ask the L2 to load ``(tensor, nbytes)`` ranges (rt_l2_prefetch on the current stream); nothing waits."""
+    if not ranges:
+        return
+    pf = _l2_ranges(ranges)
+    dev = ranges[0][0].device if device is None else device
+    _lib.check(_lib.load().rt_l2_prefetch(ctypes.addressof(pf), int(ctas), _stream(dev)), "rt_l2_prefetch")
+    _count()
 
 
 def default_splits(n: int, num_q_heads: int, num_kv_heads: int, prefix_len: int) -> int:

@@ -101,14 +101,23 @@ def test_linear_shape_checks_without_gpu():
 
 def test_l2_prefetch_struct_and_checks_without_gpu():
     import ctypes
-    assert ctypes.sizeof(_lib.L2Prefetch) == 32 and _lib.L2Prefetch.bytes.offset == 16
+    assert ctypes.sizeof(_lib.L2Ranges) == 8 + 16 * 8 + 16 * 8 and _lib.L2Ranges.bytes.offset == 136
     lib = _lib.load()
-    pf = _lib.L2Prefetch()
+    pf = _lib.L2Ranges()
+    pf.count = 1
     pf.ptr[0], pf.bytes[0] = 4096 + 8, 1 << 20  # not 16-byte aligned: refused before any launch
     fake = 1 << 20  # aligned addresses that the host side never dereferences
     rc = lib.rt_tree_attn_ex(fake, 32 * 256, 256, fake, fake, 4096 * 256, 256, 4096, fake, 32 * 256, 256, fake, 1,
                              17, 2048, None, 32, 8, 128, 1.0, 1, 0, None, 0, ctypes.addressof(pf), None, None)
     assert rc == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 4, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    pf.count = 17
+    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 4, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    pf.count = 0
+    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 0, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 4, None) == _lib.RT_OK  # nothing to request
     with pytest.raises(RuntimeError, match="CUDA"):
         kernels.tree_attention(torch.zeros(17, 32, 128), torch.zeros(8, 64, 128), torch.zeros(8, 64, 128),
                                torch.zeros(17, 1, dtype=torch.int32), 40, l2_prefetch=[(torch.zeros(64), 256)])
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kernels.l2_prefetch([(torch.zeros(64), 256)])

@@ -57,3 +57,32 @@ def test_fused_forward_is_unchanged_by_l2_warm_up():
         outs.append(ft.forward(tok, pos, bits, offset=L).clone())
     kernels.check_device_status(dev)
     assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
+
+
+@torch.inference_mode()
+def test_side_stream_warm_up_changes_no_round(monkeypatch):
+    """FusedTarget(l2_stream=True): same logits eagerly, and graph rounds equal to eager rounds without it."""
+    from retree_b200 import synthetic
+    from retree_b200.verify import TreeVerifier
+
+    monkeypatch.setenv("DDTREE_TREE_STRATEGY", "rank_gated_ngram")
+    dev = cuda()
+    cfg = qwen3_config("small", hidden_size=512, intermediate_size=1024, num_hidden_layers=3, num_attention_heads=8,
+                       num_key_value_heads=2, vocab_size=2000, tie_word_embeddings=False)
+    model = build_target(cfg, device=dev, seed=6)
+    prompt = torch.from_numpy(synthetic.context_ids(2, 120, 2000, alphabet=40))[None].to(dev)
+    drafts = [torch.from_numpy(synthetic.draft_logits(50 + r, 15, 2000, amp=6.0)).to(dev).to(torch.bfloat16)
+              for r in range(4)]
+    plain = TreeVerifier(model, tree_budget=20, max_length=400, fused=True, gemm="cublas", l2_stream=False)
+    warm = TreeVerifier(model, tree_budget=20, max_length=400, fused=True, gemm="cublas", l2_stream=True,
+                        attn_l2_prefetch=8 << 20)
+    assert warm.fused.l2_stream and not plain.fused.l2_stream
+    plain.prefill(prompt)
+    warm.prefill(prompt)
+    warm.enable_graph(True)
+    for d in drafts:
+        assert plain.round(d) == warm.round(d)
+    kernels.check_device_status(dev)
+    s = plain.start
+    assert torch.equal(plain.output_ids[: s + 1], warm.output_ids[: s + 1])
+    assert torch.equal(plain.cache.slab[:, :, :s], warm.cache.slab[:, :, :s])
