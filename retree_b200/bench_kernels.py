@@ -167,9 +167,52 @@ def linear_case(name: str, m: int, layers: int, dev) -> list[dict]:
     return rows
 
 
+def draft_case(dev, hidden: int = 4096, layers: int = 5, ctx: int = 5, prefix: int = 2048, block: int = 16,
+               vocab: int = 151936) -> list[dict]:
+    """One DFlash draft call on the fused stages (``FusedDraft``): a decode-sized call (``ctx`` new
+    context rows) and the first call of a request (the whole ``prefix`` as context rows).
+
+    Synthetic draft of the Qwen3-8B geometry (``layers`` draft layers; the draft checkpoints' layer
+    counts are not part of the reference), target embedding and lm_head of that vocabulary.
+    """
+    from torch import nn
+
+    from .draft import FusedDraft, random_draft
+
+    ids = [1, 9, 17, 25, 33][:layers]
+    draft = random_draft(hidden, layers, 32, 8, 3 * hidden, block, ids, dev)
+
+    class _Target(nn.Module):
+        pass
+
+    tgt = _Target()
+    tgt.config = type("Cfg", (), {"hidden_size": hidden})()
+    tgt.model = nn.Module()
+    tgt.model.embed_tokens = nn.Embedding(vocab, hidden, device=dev, dtype=torch.bfloat16).requires_grad_(False)
+    tgt.lm_head = nn.Linear(hidden, vocab, bias=False, device=dev, dtype=torch.bfloat16).requires_grad_(False)
+    fd = FusedDraft(draft, tgt, capacity=prefix + 4 * block)
+    g = torch.Generator(device=dev).manual_seed(0)
+    block_ids = torch.randint(0, vocab, (block,), device=dev, generator=g)
+    w_layer = sum(p.numel() * 2 for L in fd.layers for p in (L.qkv_w, L.o_w, L.gate_up_w, L.down_w))
+    rows = []
+    for c, start in ((ctx, prefix), (prefix, prefix)):
+        th = torch.randn((c, len(ids) * hidden), device=dev, generator=g).to(torch.bfloat16)
+
+        def call():
+            fd.length = start - c
+            fd.forward(block_ids, th, start)
+
+        us = graph_time_us(call, reps=10)
+        kernels.check_device_status(dev)
+        w = w_layer + fd.fc_w.numel() * 2 + fd.lm_head.numel() * 2
+        rows.append(dict(kernel="draft_forward", context_rows=c, start=start, block=block, draft_layers=layers,
+                         us_per_call=us, weight_bytes=w, gbs_weights=w / us / 1e3, hbm_frac=w / us / 1e3 / peaks()[0]))
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("mode", choices=("sweep", "single", "parts", "linear"))
+    ap.add_argument("mode", choices=("sweep", "single", "parts", "linear", "draft"))
     ap.add_argument("--m", default="17,65,257")
     ap.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
     ap.add_argument("--prefix", type=int, default=4096)
@@ -194,6 +237,9 @@ def main():
         torch.cuda.synchronize()
         kernels.check_device_status(dev)
         print(json.dumps(dict(ok=True, budget=a.budget, prefix=a.prefix)))
+    elif a.mode == "draft":
+        for row in draft_case(dev, prefix=a.prefix):
+            print(json.dumps(row), flush=True)
     elif a.mode == "linear":
         for m in (int(x) for x in a.m.split(",")):
             for name in a.shapes.split(","):

@@ -233,3 +233,62 @@ class FusedDraft:
         if return_hidden:
             return xn
         return torch.mm(xn[b - horizon:], self.lm_head.t(), out=self.logits[:horizon])
+
+
+class _DraftAttention(torch.nn.Module):
+    pass
+
+
+class _DraftLayer(torch.nn.Module):
+    pass
+
+
+class DraftLayout(torch.nn.Module):
+    """A DFlash draft's parameters under the reference module's names (model/dflash.py:33-75, :127-139,
+    :176-209), with no forward of its own: what ``FusedDraft`` reads.  For synthetic-weight benchmarks."""
+
+
+def random_draft(hidden: int, layers: int, heads: int, kv_heads: int, inter: int, block_size: int,
+                 target_layer_ids, device, seed: int = 0, rope_theta: float = 1_000_000.0,
+                 max_positions: int = 40960) -> DraftLayout:
+    """A bf16 draft with the reference's layout and N(0, 1/fan_in) projections (norm scales 1)."""
+    from torch import nn
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RMSNorm, Qwen3RotaryEmbedding
+
+    cfg = Qwen3Config(hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers,
+                      num_attention_heads=heads, num_key_value_heads=kv_heads, head_dim=128, rms_norm_eps=1e-6,
+                      max_position_embeddings=max_positions, rope_theta=rope_theta)
+    cfg.block_size = block_size
+    g = torch.Generator(device="cpu").manual_seed(seed)
+
+    def lin(i, o):
+        m = nn.Linear(i, o, bias=False, device="meta")
+        m.weight = nn.Parameter((torch.randn((o, i), generator=g) * i ** -0.5).to(torch.bfloat16).to(device),
+                                requires_grad=False)
+        return m
+
+    def norm(n):
+        return Qwen3RMSNorm(n, eps=cfg.rms_norm_eps).to(device=device, dtype=torch.bfloat16).requires_grad_(False)
+
+    d = DraftLayout()
+    d.config = cfg
+    d.block_size = block_size
+    d.target_layer_ids = list(target_layer_ids)
+    d.layers = nn.ModuleList()
+    for _ in range(layers):
+        L = _DraftLayer()
+        a = _DraftAttention()
+        a.q_proj, a.k_proj, a.v_proj = lin(hidden, heads * 128), lin(hidden, kv_heads * 128), lin(hidden, kv_heads * 128)
+        a.o_proj = lin(heads * 128, hidden)
+        a.q_norm, a.k_norm = norm(128), norm(128)
+        a.scaling = 128 ** -0.5
+        L.self_attn = a
+        L.mlp = nn.Module()
+        L.mlp.gate_proj, L.mlp.up_proj, L.mlp.down_proj = lin(hidden, inter), lin(hidden, inter), lin(inter, hidden)
+        L.input_layernorm, L.post_attention_layernorm = norm(hidden), norm(hidden)
+        d.layers.append(L)
+    d.fc = lin(len(d.target_layer_ids) * hidden, hidden)
+    d.hidden_norm, d.norm = norm(hidden), norm(hidden)
+    d.rotary_emb = Qwen3RotaryEmbedding(cfg, device=device)
+    return d

@@ -209,3 +209,14 @@ def test_side_stream_warm_up_plan(fake_kernels):
         for ranges in L.warm.values():
             for t, b in ranges:
                 assert 0 < b <= min(budget, nb(t)) and t.is_contiguous()
+
+
+@torch.inference_mode()
+def test_synthetic_draft_layout_runs_through_the_fused_draft(fake_kernels):
+    """``draft.random_draft`` (the benchmark's synthetic draft) has the layout ``FusedDraft`` reads."""
+    d = draft_mod.random_draft(256, 2, 4, 2, 512, 8, [1, 3], "cpu")
+    assert draft_mod.supports(d)
+    fd = draft_mod.FusedDraft(d, _Target(256, 300, seed=2), capacity=128)
+    th = torch.randn((12, 512)).to(BF)
+    logits = fd.forward(torch.full((8,), 5, dtype=torch.int64), th, 12)
+    assert logits.shape == (7, 300) and bool(torch.isfinite(logits.float()).all())
