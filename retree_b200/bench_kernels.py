@@ -115,12 +115,15 @@ def parts(dev) -> list[dict]:
         out.append(dict(kernel="draft_topk", budget=budget, rows=15, vocab=151936, us=us,
                         gbs=15 * 151936 * 2 / us / 1e3))
         lp, ids, _ = kernels.draft_topk(logits, budget)
-        buf = {}
-        tree = kernels.tree_build(lp, ids, budget, "rank_gated_ngram", NgramParams.from_env({}), ctx=ctx, out=None)
-        buf.update(tree)
-        us = graph_time_us(lambda: kernels.tree_build(lp, ids, budget, "rank_gated_ngram",
-                                                      NgramParams.from_env({}), ctx=ctx, out=buf))
-        out.append(dict(kernel="tree_build", strategy="rank_gated_ngram", budget=budget, context=2049, us=us))
+        # the heap strategy has no n-gram table and no bonus lookups: the difference
+        # bounds what the per-round table rebuild and the lookups cost
+        for strategy in ("rank_gated_ngram", "heap"):
+            buf = {}
+            tree = kernels.tree_build(lp, ids, budget, strategy, NgramParams.from_env({}), ctx=ctx, out=None)
+            buf.update(tree)
+            us = graph_time_us(lambda: kernels.tree_build(lp, ids, budget, strategy, NgramParams.from_env({}),
+                                                          ctx=ctx, out=buf))
+            out.append(dict(kernel="tree_build", strategy=strategy, budget=budget, context=2049, us=us))
     slab = torch.randn((72, 8, 4096 + 17, 128), device=dev).to(torch.bfloat16)
     keep = torch.tensor([0, 1, 3, 7, 9, 12, 15], dtype=torch.long, device=dev)
     us = graph_time_us(lambda: kernels.kv_compact(slab, 4096, keep))
