@@ -16,7 +16,10 @@ masking_utils.py:827-829):
   * the dense additive mask the reference's ``compile_ddtree_tree`` writes
     (ddtree.py:629-640): its tree block is packed to bits on the device;
   * no mask (prefill / plain decode): causal attention of the new tokens over
-    the cache, run as a chain-shaped tree.
+    the cache, run as a chain-shaped tree -- unless the caller asks for
+    ``is_causal=False`` (the DFlash draft's attention, model/dflash.py:47 and
+    its callers' kwargs), which the SDPA backend honours the same way
+    (sdpa_attention.py:64-77): then every new token sees every key.
 """
 
 from __future__ import annotations
@@ -60,9 +63,19 @@ def causal_bits(n: int, device) -> torch.Tensor:
     return b
 
 
-def _bits_for(mask, n: int, key_len: int, device):
+def full_bits(n: int, device) -> torch.Tensor:
+    """Every node sees every node of the block, int32 ``[n, ceil(n/32)]`` (bits past n are ignored)."""
+    key = ("full", torch.device(device).index, n)
+    b = _CAUSAL_BITS.get(key)
+    if b is None:
+        b = torch.full((n, (n + 31) // 32), -1, dtype=torch.int32, device=device)
+        _CAUSAL_BITS[key] = b
+    return b
+
+
+def _bits_for(mask, n: int, key_len: int, device, causal: bool = True):
     if mask is None:
-        return causal_bits(n, device), None
+        return (causal_bits(n, device) if causal else full_bits(n, device)), None
     bits = getattr(mask, TreeMask.BITS_ATTR, None)
     if bits is not None:
         return bits, getattr(mask, TreeMask.PREFIX_DEV_ATTR, None)
@@ -90,7 +103,11 @@ def tree_attention_forward(module, query: torch.Tensor, key: torch.Tensor, value
     if query.shape[0] != 1:
         raise RuntimeError("retree_tree attention verifies one sequence (batch 1)")
     n = query.shape[2]
-    bits, prefix_dev = _bits_for(attention_mask, n, key.shape[2], query.device)
+    # the SDPA backend's rule: the call's is_causal, else the module's (default causal)
+    causal = kwargs.get("is_causal", None)
+    if causal is None:
+        causal = getattr(module, "is_causal", True)
+    bits, prefix_dev = _bits_for(attention_mask, n, key.shape[2], query.device, causal=bool(causal))
     if PROFILE is not None:
         ev0 = torch.cuda.Event(enable_timing=True)
         ev1 = torch.cuda.Event(enable_timing=True)

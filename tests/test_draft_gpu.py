@@ -156,3 +156,23 @@ def test_ddtree_generate_with_a_draft_module_commits_greedy_tokens(monkeypatch, 
     if got[: len(greedy)] != greedy[: len(got)]:
         first = next(i for i, (a, b) in enumerate(zip(got, greedy)) if a != b)
         assert first >= 8 and margins[first] < 2e-2, (first, margins[first])
+
+
+@torch.inference_mode()
+def test_attention_backend_runs_the_draft_attention_non_causal():
+    """The HF backend with no mask and is_causal=False (the draft's call) matches SDPA without a mask."""
+    import torch.nn.functional as F
+
+    dev = cuda()
+    g = torch.Generator(device=dev).manual_seed(3)
+    n, S = 16, 300
+    q = torch.randn((1, 32, n, 128), device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn((1, 8, S, 128), device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn((1, 8, S, 128), device=dev, generator=g).to(torch.bfloat16)
+    mod = torch.nn.Module()
+    mod.is_causal = False
+    out, _ = attention.tree_attention_forward(mod, q, k, v, None, scaling=128 ** -0.5, is_causal=False)
+    ref = F.scaled_dot_product_attention(q.float(), k.float().repeat_interleave(4, 1),
+                                         v.float().repeat_interleave(4, 1), scale=128 ** -0.5)
+    err = (out[0].float() - ref[0].transpose(0, 1)).abs()
+    assert float(err.max()) < 2e-2 and float(err.mean()) < 1e-3

@@ -69,7 +69,11 @@ def fake_kernels(monkeypatch):
 
     def tree_attention(q, k, v, bits, prefix_len, scale=None, out=None, num_splits=0, path=0, prefix_len_dev=None,
                        kv_capacity=None, l2_prefetch=None):
+        if q.dim() == 4:  # HF's [1, Hq, n, D] / [1, Hkv, S, D], as the real wrapper takes them
+            q, k, v = q[0].transpose(0, 1), k[0], v[0]
         n, hq, d = q.shape
+        if out is None:
+            out = torch.empty((n, hq, d), dtype=BF)
         L = int(prefix_len) + (0 if prefix_len_dev is None else int(prefix_len_dev[0]))
         hkv = k.shape[0]
         words = bits.numpy().view(np.uint32)
@@ -220,3 +224,28 @@ def test_synthetic_draft_layout_runs_through_the_fused_draft(fake_kernels):
     th = torch.randn((12, 512)).to(BF)
     logits = fd.forward(torch.full((8,), 5, dtype=torch.int64), th, 12)
     assert logits.shape == (7, 300) and bool(torch.isfinite(logits.float()).all())
+
+
+@torch.inference_mode()
+@pytest.mark.parametrize("module_causal,call_causal,want_causal", [
+    (True, None, True), (False, None, False), (True, False, False), (False, True, True)])
+def test_attention_backend_honours_is_causal_without_a_mask(fake_kernels, module_causal, call_causal, want_causal):
+    """No mask: causal unless the call (else the module) says is_causal=False, as HF's SDPA backend decides
+    (the DFlash draft attends to every key, model/dflash.py:47)."""
+    from retree_b200 import attention
+
+    g = torch.Generator().manual_seed(0)
+    n, S = 6, 20
+    q = torch.randn((1, 4, n, 128), generator=g).to(BF)
+    k = torch.randn((1, 2, S, 128), generator=g).to(BF)
+    v = torch.randn((1, 2, S, 128), generator=g).to(BF)
+    mod = torch.nn.Module()
+    mod.is_causal = module_causal
+    kw = {} if call_causal is None else {"is_causal": call_causal}
+    out, _ = attention.tree_attention_forward(mod, q, k, v, None, scaling=128 ** -0.5, **kw)
+    mask = torch.zeros((n, S))
+    if want_causal:
+        mask[:, S - n:] = torch.triu(torch.full((n, n), float("-inf")), diagonal=1)
+    ref = F.scaled_dot_product_attention(q.float(), k.float().repeat_interleave(2, 1),
+                                         v.float().repeat_interleave(2, 1), attn_mask=mask, scale=128 ** -0.5)
+    assert float((out[0].float() - ref[0].transpose(0, 1)).abs().max()) < 2e-2
