@@ -231,6 +231,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp == kProducerWarp) {
     // ---------------- TMA producer: lane 0 Q and K, lane 1 V ----------------
+    // with an L2 warm-up in flight the K/V stream (read once per round) is
+    // loaded evict-first, so it does not push the warmed lines out
+    const bool kv_hint = p.pf.count > 0;
+    const uint64_t kv_policy = kv_hint ? l2_policy_evict_first() : 0ull;
     if (lane == 0) {
       auto issue_q = [&] {
         pdl_wait();
@@ -257,8 +261,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int key0 = static_cast<int>((b0 + j) * kBN);
         unsigned char* kd = smem + kOffK + st * kTile;
         mbar_arrive_expect_tx(&bar.full_k[st], kTile);
-        tma_load_3d(kd, &tmap_k, &bar.full_k[st], 0, key0, kvh);
-        tma_load_3d(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh);
+        if (kv_hint) {
+          tma_load_3d_hint(kd, &tmap_k, &bar.full_k[st], 0, key0, kvh, kv_policy);
+          tma_load_3d_hint(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh, kv_policy);
+        } else {
+          tma_load_3d(kd, &tmap_k, &bar.full_k[st], 0, key0, kvh);
+          tma_load_3d(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh);
+        }
         issued = j + 1;
       }
       if (!q_issued) issue_q();
@@ -277,8 +286,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int key0 = static_cast<int>((b0 + j) * kBN);
         unsigned char* vd = smem + kOffV + st * kTile;
         mbar_arrive_expect_tx(&bar.full_v[st], kTile);
-        tma_load_3d(vd, &tmap_v, &bar.full_v[st], 0, key0, kvh);
-        tma_load_3d(vd + kHalf, &tmap_v, &bar.full_v[st], 64, key0, kvh);
+        if (kv_hint) {
+          tma_load_3d_hint(vd, &tmap_v, &bar.full_v[st], 0, key0, kvh, kv_policy);
+          tma_load_3d_hint(vd + kHalf, &tmap_v, &bar.full_v[st], 64, key0, kvh, kv_policy);
+        } else {
+          tma_load_3d(vd, &tmap_v, &bar.full_v[st], 0, key0, kvh);
+          tma_load_3d(vd + kHalf, &tmap_v, &bar.full_v[st], 64, key0, kvh);
+        }
         issued = j + 1;
       }
       if (*abort_flag)
