@@ -93,9 +93,18 @@ __device__ void block_select(const uint32_t* keys, const int* idx_in, int idx_ba
     sh.hist[tid] = 0;  // kTopkThreads == 256 bins
     __syncthreads();
     const uint32_t prefix = sh.prefix;
-    for (int i = tid; i < len; i += kTopkThreads) {
-      const uint32_t key = keys[i];
-      if (((key ^ prefix) & himask) == 0) atomicAdd(&sh.hist[(key >> shift) & 255u], 1u);
+    // Warp-aggregated counting: logits share their leading key bytes (sign and
+    // exponent), so most live keys of a pass land in a handful of bins; one
+    // atomic per distinct bin per warp instead of one per key.
+    for (int base = 0; base < len; base += kTopkThreads) {  // same trip count on every lane
+      const int i = base + tid;
+      uint32_t bin = 256u;  // no bin
+      if (i < len) {
+        const uint32_t key = keys[i];
+        if (((key ^ prefix) & himask) == 0) bin = (key >> shift) & 255u;
+      }
+      const uint32_t peers = __match_any_sync(0xFFFFFFFFu, bin);
+      if (bin < 256u && (tid & 31) == __ffs(peers) - 1) atomicAdd(&sh.hist[bin], static_cast<uint32_t>(__popc(peers)));
     }
     __syncthreads();
     if (tid < 32) {
@@ -271,6 +280,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(int vocab, int
   int* sel_idx = reinterpret_cast<int*>(sel_key + sort_len);
   block_select(keys, idx, 0, total, k, sel_key, sel_idx, sh);
   // pack (key desc, index asc) into 64-bit keys, pad to the power-of-two length
+  // (sort_len <= 1024: at most 4 per thread; threads past a short length idle)
   unsigned long long packed[4];
   const int per = sort_len / kTopkThreads > 0 ? sort_len / kTopkThreads : 1;
   for (int j = 0; j < per; ++j) {
@@ -331,7 +341,7 @@ static TopkPlan topk_plan(int rows, int vocab, int k) {
   for (int c = 0; c < p.n_chunks; ++c) p.total += std::min(k, std::min(cl, vocab - c * cl));
   p.sort_len = 1;
   while (p.sort_len < k) p.sort_len <<= 1;
-  p.sort_len = std::max(p.sort_len, kTopkThreads);
+  p.sort_len = std::max(p.sort_len, 32);  // a k-element bitonic network, not a 256-element one
   const size_t cand = static_cast<size_t>(rows) * p.n_chunks * k;
   p.ws_key = 0;
   p.ws_idx = align_up(cand * 4, 256);
