@@ -44,6 +44,7 @@ struct BuildArgs {
   int table_len;
   int hash_slots;    // power of two (>= 64) when there is an n-gram table, else 0
   int stage_topk;    // top-k staged in shared memory
+  int log1p_staged;  // leading log1p-table entries copied to shared memory
   int mask_in_smem;  // ancestor rows kept in shared memory
   int64_t* node_tokens;
   int64_t* node_depths;
@@ -127,13 +128,13 @@ __device__ int ngram_count(const uint32_t* table, int mask, const int* ctx, cons
 struct Layout {
   size_t f_aug, f_logw, f_bonus, f_inc, f_tok, f_parent, f_rank, f_depth;
   size_t n_tail, n_rank, n_depth, n_parent, n_mask;
-  size_t ctx, table, s_lp, s_ids, total;
+  size_t ctx, table, s_lp, s_ids, s_log1p, total;
 };
 
 __host__ __device__ inline size_t al16(size_t x) { return (x + 15) & ~static_cast<size_t>(15); }
 
 __host__ __device__ inline Layout make_layout(int budget, int win, int hash_slots, int rows, int k, int words,
-                                              bool stage, bool mask_smem) {
+                                              bool stage, bool mask_smem, int log1p_staged) {
   Layout L{};
   const size_t FC = static_cast<size_t>(budget) + 2, NN = static_cast<size_t>(budget) + 1;
   size_t o = 0;
@@ -159,6 +160,7 @@ __host__ __device__ inline Layout make_layout(int budget, int win, int hash_slot
   L.table = put(4 * static_cast<size_t>(hash_slots > 0 ? hash_slots : 1));
   L.s_lp = stage ? put(4 * static_cast<size_t>(rows) * k) : 0;
   L.s_ids = stage ? put(8 * static_cast<size_t>(rows) * k) : 0;
+  L.s_log1p = log1p_staged > 0 ? put(8 * static_cast<size_t>(log1p_staged)) : 0;
   L.total = o;
   return L;
 }
@@ -206,7 +208,7 @@ __global__ void __launch_bounds__(kBuildThreads) tree_build_kernel(BuildArgs a) 
     ctx_src = a.ctx + (Lctx - win);
   }
   const Layout Ly = make_layout(B, a.win_cap, a.hash_slots, a.rows, a.k, a.mask_words, a.stage_topk != 0,
-                                a.mask_in_smem != 0);
+                                a.mask_in_smem != 0, a.log1p_staged);
   double* f_aug = reinterpret_cast<double*>(smem + Ly.f_aug);
   double* f_logw = reinterpret_cast<double*>(smem + Ly.f_logw);
   double* f_bonus = reinterpret_cast<double*>(smem + Ly.f_bonus);
@@ -225,6 +227,8 @@ __global__ void __launch_bounds__(kBuildThreads) tree_build_kernel(BuildArgs a) 
   uint32_t* table = reinterpret_cast<uint32_t*>(smem + Ly.table);
   const float* lp = a.stage_topk ? reinterpret_cast<const float*>(smem + Ly.s_lp) : a.lp;
   const int64_t* ids = a.stage_topk ? reinterpret_cast<const int64_t*>(smem + Ly.s_ids) : a.ids;
+  double* s_log1p = reinterpret_cast<double*>(smem + Ly.s_log1p);
+  for (int i = tid; i < a.log1p_staged; i += kBuildThreads) s_log1p[i] = a.log1p_table[i];
 
   // ---- prologue: window, n-gram counts, staged top-k ----
   const int hmask = a.hash_slots - 1;
@@ -285,7 +289,8 @@ __global__ void __launch_bounds__(kBuildThreads) tree_build_kernel(BuildArgs a) 
     if ((q1 ? on1 : on0) && p <= tail_size && p <= tl_ptr[7])
       c = ngram_count(table, hmask, ctx, tl_ptr, tl_ptr[7], p, static_cast<int>(q1 ? tok1 : tok0));
     // each lane fetches its own order's log1p(count), so the loads overlap
-    const double base = a.use_log_count ? a.log1p_table[min(c, a.table_len - 1)] : 1.0;
+    const int ci = min(c, a.table_len - 1);
+    const double base = !a.use_log_count ? 1.0 : (ci < a.log1p_staged ? s_log1p[ci] : a.log1p_table[ci]);
     const int tla = t0[7], tlb = t1[7];
     double sa = 0.0, sb = 0.0;
     for (int n = 2; n <= a.max_n; ++n) {
@@ -542,12 +547,26 @@ extern "C" int rt_tree_build(const float* top_logp, const int64_t* top_ids, int 
   const int stage_rows = rows > 0 ? rows : 1;
   a.mask_in_smem = 1;
   a.stage_topk = 1;
-  if (make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, true, true).total > kSmemBudget)
+  a.log1p_staged = 0;
+  if (make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, true, true, 0).total > kSmemBudget)
     a.stage_topk = 0;
-  if (make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, a.stage_topk, true).total > kSmemBudget)
+  if (make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, a.stage_topk, true, 0).total > kSmemBudget)
     a.mask_in_smem = 0;
-  const size_t smem =
-      make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, a.stage_topk, a.mask_in_smem).total;
+  // then the log1p table (one lookup per bonus, on the expansion's critical
+  // path): all of it when it fits, else its head (small counts are the common case)
+  if (use_log_count) {
+    for (int want : {table_len, 256}) {
+      want = want < table_len ? want : table_len;
+      if (make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, a.stage_topk, a.mask_in_smem, want)
+              .total <= kSmemBudget) {
+        a.log1p_staged = want;
+        break;
+      }
+    }
+  }
+  const size_t smem = make_layout(budget, a.win_cap, slots, stage_rows, k, mask_words, a.stage_topk,
+                                  a.mask_in_smem, a.log1p_staged)
+                          .total;
   if (smem > kSmemBudget) return RT_ERR_UNSUPPORTED;
   if (rows == 0) a.stage_topk = 0;
   set_smem_limit(tree_build_kernel, smem);
