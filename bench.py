@@ -82,6 +82,8 @@ def parse():
                     help="MB of the following projections' weights each attention launch warms in L2")
     ap.add_argument("--l2-stream", action="store_true",
                     help="warm the next projection's weights in L2 from a side stream next to each launch")
+    ap.add_argument("--exchange", choices=("nccl", "p2p"), default="nccl",
+                    help="split workloads: attention-output all-gather over NCCL or over peer memory")
     return ap.parse_args()
 
 
@@ -284,7 +286,8 @@ def run_ours(args, wl, rank, world, local_rank):
     def fresh():
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
                          fused=not args.hf_forward, gemm=args.gemm,
-                         attn_l2_prefetch=int(args.attn_l2_prefetch * 2**20), l2_stream=args.l2_stream)
+                         attn_l2_prefetch=int(args.attn_l2_prefetch * 2**20), l2_stream=args.l2_stream,
+                         exchange=args.exchange)
         if wl.get("split"):
             v.prefill_random(plen, seed=req)
         else:
@@ -426,6 +429,9 @@ def run_ours(args, wl, rank, world, local_rank):
     v.graph = None
     v2.graph = None
     torch.cuda.synchronize()
+    for vv in (v, v2):  # peer-memory exchanges unmap on every rank together
+        if vv.fused is not None and vv.fused.peer is not None:
+            vv.fused.peer.close()
     if rank != 0:
         return
     hbm_peak, tf_peak, peak_kind = measured_peaks()
@@ -454,7 +460,8 @@ def run_ours(args, wl, rank, world, local_rank):
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
                    "projections": projections,
                    "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
-                   "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer)"
+                   "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "
+                                   f"{'peer memory' if args.exchange == 'p2p' else 'NCCL'})"
                                    if wl.get("split") else f"dp{world} (one request per GPU)" + (
                                        ", recovery-delta all-gather per step" if world > 1 else "")),
                    "l2": "inputs > L2 (8 GB of weights and the KV cache stream every round)",

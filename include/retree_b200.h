@@ -171,6 +171,39 @@ int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_head_stride, 
                     int head_dim, float scale, int num_splits, int path, void* workspace, size_t workspace_bytes,
                     const rt_l2_ranges* prefetch, int* status, rt_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * Attention-output exchange of a KV-head split over NVLink peer memory.
+ * Replaces the NCCL all-gather of the attention outputs before o_proj when
+ * one long request is split by KV head over several GPUs
+ * (retree_b200/headsplit.py; the reference runs one request on one GPU and
+ * has no counterpart).  Buffers are shared between the ranks' processes with
+ * CUDA IPC (plain peer mappings, no multicast).
+ *
+ * rt_ipc_alloc: cudaMalloc'd, zeroed device buffer of `bytes` and its 64-byte
+ *   IPC handle; rt_ipc_free releases it.  rt_ipc_open maps a peer's handle
+ *   (peer access enabled lazily), rt_ipc_close unmaps it.
+ * rt_peer_epoch_step: *epoch_dev += add on the stream (one per forward).
+ * rt_peer_signal: after this rank's attention rows are in its buffer, stores
+ *   *epoch_dev + epoch_add into slot `rank` of every rank's int64 flag array
+ *   (peer_flags[p] = rank p's array as mapped here), release at system scope.
+ * rt_peer_gather: for every source rank s, waits (bounded; RT_DEV_WAIT_TIMEOUT
+ *   in *status, rows not copied) until flags_local[s] >= *epoch_dev +
+ *   epoch_add, then copies rows [0, rows) of peer_bufs[s] (row stride src_ld
+ *   bytes, row_bytes each) to out + s*row_bytes (row stride out_ld).  Sizes
+ *   and strides are multiples of 16 bytes, pointers 16-byte aligned,
+ *   world <= 8.
+ * ---------------------------------------------------------------------- */
+int rt_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int rt_ipc_free(void* ptr);
+int rt_ipc_open(const void* handle, void** ptr);
+int rt_ipc_close(void* ptr);
+int rt_peer_epoch_step(int64_t* epoch_dev, int64_t add, rt_stream_t stream);
+int rt_peer_signal(void* const* peer_flags, int world, int rank, const int64_t* epoch_dev, int64_t epoch_add,
+                   rt_stream_t stream);
+int rt_peer_gather(void* const* peer_bufs, int world, int rows, int64_t row_bytes, int64_t src_ld, void* out,
+                   int64_t out_ld, const int64_t* flags_local, const int64_t* epoch_dev, int64_t epoch_add,
+                   int* status, rt_stream_t stream);
+
 /* Number of key splits rt_tree_attn chooses for this shape (num_splits = 0). */
 int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len);
 

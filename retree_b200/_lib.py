@@ -36,6 +36,13 @@ SIGNATURES = {
                              _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P, _P]),
     "rt_tree_attn_default_splits": (_I, [_I, _I, _I, _I64]),
     "rt_l2_prefetch": (_I, [_P, _I, _P]),
+    "rt_ipc_alloc": (_I, [_SZ, _P, _P]),
+    "rt_ipc_free": (_I, [_P]),
+    "rt_ipc_open": (_I, [_P, _P]),
+    "rt_ipc_close": (_I, [_P]),
+    "rt_peer_epoch_step": (_I, [_P, _I64, _P]),
+    "rt_peer_signal": (_I, [_P, _I, _I, _P, _I64, _P]),
+    "rt_peer_gather": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
     "rt_tree_attn_noalloc_max_bytes": (_SZ, []),
     "rt_tree_attn_noalloc": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                                   _I, _I, _I, _F, _I, _I, _P, _P]),

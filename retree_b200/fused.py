@@ -115,7 +115,7 @@ class _Layer:
 class FusedTarget:
     def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto",
                  capture_layers=None, attn_l2_prefetch: int | None = None, l2_stream: bool | None = None,
-                 l2_stream_budget: int = 64 << 20):
+                 l2_stream_budget: int = 64 << 20, exchange: str = "nccl"):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -217,6 +217,19 @@ class FusedTarget:
                           "o": [(L.gate_up_w[head // nb(L.gate_up_w[0]):], min(gu - head, cap))] if gu > head else [],
                           "gate_up": [(L.down_w, min(nb(L.down_w), cap))],
                           "down": [(nxt, min(nb(nxt), cap))]}
+        # under a KV-head split: the attention outputs' all-gather before o_proj,
+        # NCCL ("nccl") or this package's peer-memory exchange ("p2p", retree_b200.peer)
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        self.peer = None
+        split = self.layers[0].split
+        if exchange == "p2p" and split is not None and split[1] > 1:
+            from .peer import PeerExchange
+            if len(self.layers) % 2:
+                raise RuntimeError("the peer exchange alternates two slots by layer: it needs an even layer count")
+            group, world, rank = split
+            self.peer = PeerExchange(group, rank, world, self.n_max, hq * self.head_dim, len(self.layers), dev)
+            self.attn_full = torch.empty((self.n_max, world * hq * self.head_dim), dtype=torch.bfloat16, device=dev)
         if gemm not in ("auto", "tcgen05", "cublas"):
             raise ValueError("gemm must be 'auto', 'tcgen05' or 'cublas'")
         self.gemm = gemm
@@ -378,6 +391,8 @@ class FusedTarget:
         splits = self._splits(n)
         res, xn = self.residual[:n], self.xnorm[:n]
         warm = self._warm if self.l2_stream else (lambda L, kind: None)
+        if self.peer is not None:
+            self.peer.step()
         for L in self.layers:
             if L.index == 0:
                 kernels.embed_rmsnorm(ids, self.embed, L.in_norm, L.eps_in, res, xn)
@@ -390,16 +405,21 @@ class FusedTarget:
             self._qkv(L, xn, positions, offset, offset_dev)
             kc, vc = slab[2 * L.index], slab[2 * L.index + 1]
             warm(L, "attn")
+            # this rank's heads go straight into its exchange slot under the peer exchange
+            attn_out = self.attn[:n] if self.peer is None else self.peer.slot(L.index, n).view(n, L.hq, -1)
             if offset_dev is not None:
-                kernels.tree_attention(self.q[:n], kc, vc, bits, cap - n, scale=L.scale, out=self.attn[:n],
+                kernels.tree_attention(self.q[:n], kc, vc, bits, cap - n, scale=L.scale, out=attn_out,
                                        num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap,
                                        l2_prefetch=L.l2pf)
             else:
                 kernels.tree_attention(self.q[:n], kc[:, : offset + n], vc[:, : offset + n], bits, offset,
-                                       scale=L.scale, out=self.attn[:n], num_splits=splits, kv_capacity=cap,
+                                       scale=L.scale, out=attn_out, num_splits=splits, kv_capacity=cap,
                                        l2_prefetch=L.l2pf)
-            attn = self.attn[:n]
-            if L.split is not None:
+            attn = attn_out
+            if self.peer is not None:
+                self.peer.signal(L.index)
+                attn = self.peer.gather(L.index, n, self.attn_full[:n])
+            elif L.split is not None:
                 group, world, _ = L.split
                 attn = gather_heads(attn.unsqueeze(0), group, world)[0]
             warm(L, "o")

@@ -58,7 +58,7 @@ class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
                  temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None,
                  gemm: str = "auto", fused_draft: bool = False, attn_l2_prefetch: int | None = None,
-                 l2_stream: bool | None = None):
+                 l2_stream: bool | None = None, exchange: str = "nccl"):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -118,7 +118,7 @@ class TreeVerifier:
                      and not hasattr(target, "_rt_local_kv_heads"))
         self.fused = (fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm,
                                             capture_layers=target_layer_ids, attn_l2_prefetch=attn_l2_prefetch,
-                                            l2_stream=l2_stream)
+                                            l2_stream=l2_stream, exchange=exchange)
                       if fused else None)
         # draft forward: the DFlash module (reference layout) on the fused stages
         # (retree_b200.draft.FusedDraft) when asked for and supported

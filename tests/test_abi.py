@@ -121,3 +121,23 @@ def test_l2_prefetch_struct_and_checks_without_gpu():
                                torch.zeros(17, 1, dtype=torch.int32), 40, l2_prefetch=[(torch.zeros(64), 256)])
     with pytest.raises(RuntimeError, match="CUDA"):
         kernels.l2_prefetch([(torch.zeros(64), 256)])
+
+
+def test_peer_exchange_argument_checks_without_gpu():
+    import ctypes
+    lib = _lib.load()
+    two = (ctypes.c_void_p * 2)(1 << 20, 2 << 20)
+    bad = (ctypes.c_void_p * 2)(1 << 20, (2 << 20) + 8)  # not 16-byte aligned
+    epoch = ctypes.c_void_p(3 << 20)
+    assert lib.rt_peer_signal(bad, 2, 0, epoch, 0, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_peer_signal(two, 2, 2, epoch, 0, None) == _lib.RT_ERR_INVALID_ARGUMENT  # rank out of range
+    assert lib.rt_peer_signal(two, 9, 0, epoch, 0, None) == _lib.RT_ERR_INVALID_ARGUMENT  # more than 8 ranks
+    out = ctypes.c_void_p(4 << 20)
+    # row bytes not a multiple of 16, destination narrower than world * row, missing flags
+    assert lib.rt_peer_gather(two, 2, 4, 24, 32, out, 64, epoch, epoch, 0, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_peer_gather(two, 2, 4, 32, 32, out, 48, epoch, epoch, 0, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_peer_gather(two, 2, 4, 32, 32, out, 64, None, epoch, 0, None, None) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_peer_gather(two, 2, 0, 32, 32, out, 64, epoch, epoch, 0, None, None) == _lib.RT_OK  # no rows
+    assert lib.rt_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), (ctypes.c_ubyte * 64)()) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == _lib.RT_ERR_INVALID_ARGUMENT
+    assert lib.rt_peer_epoch_step(None, 1, None) == _lib.RT_ERR_INVALID_ARGUMENT

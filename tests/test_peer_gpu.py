@@ -1,0 +1,123 @@
+"""The KV-head split's attention-output exchange over peer memory (two GPUs; skipped on one).
+
+``PeerExchange`` (rt_peer_signal / rt_peer_gather over CUDA-IPC mappings) must
+deliver every rank's rows in head order, layer after layer and forward after
+forward (epochs from the device counter, two alternating slots), and the fused
+verify forward of a split target must give the same logits with it as with the
+NCCL all-gather.  NVLS is off (NCCL_NVLS_ENABLE=0); the exchange itself uses
+plain peer mappings.
+"""
+
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.late]
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _worker(r, world, port, q):
+    os.environ.update(RANK=str(r), WORLD_SIZE=str(world), LOCAL_RANK=str(r), LOCAL_WORLD_SIZE=str(world),
+                      MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    ex = []
+    try:
+        import numpy as np
+        import torch.distributed as dist
+
+        from oracle import tree as ot
+        from retree_b200 import distributed as rdist
+        from retree_b200 import fused, headsplit, kernels, synthetic
+        from retree_b200.cache import TreeKVCache
+        from retree_b200.peer import PeerExchange
+        from retree_b200.target import build_target, qwen3_config
+
+        rdist.init(timeout_s=120, backend="nccl")
+        dev = torch.device("cuda", r)
+        results = {}
+        # 1. the exchange alone: rank-tagged rows, 4 layers x 3 forwards
+        rows, cols, layers = 37, 256, 4
+        pe = PeerExchange(None, r, world, 64, cols, layers, dev)
+        ex.append(pe)
+        out = torch.empty((64, world * cols), dtype=torch.bfloat16, device=dev)
+        ok = True
+        with torch.inference_mode():
+            for f in range(3):
+                pe.step()
+                for layer in range(layers):
+                    tag = float(1000 * f + 10 * layer + r)
+                    vals = tag + torch.arange(rows * cols, device=dev, dtype=torch.float32).view(rows, cols) % 7
+                    pe.slot(layer, rows).copy_(vals.to(torch.bfloat16))
+                    pe.signal(layer)
+                    pe.gather(layer, rows, out[:rows])
+                    torch.cuda.synchronize(dev)
+                    for s in range(world):
+                        want = (float(1000 * f + 10 * layer + s)
+                                + torch.arange(rows * cols, device=dev, dtype=torch.float32).view(rows, cols) % 7)
+                        ok &= bool(torch.equal(out[:rows, s * cols: (s + 1) * cols], want.to(torch.bfloat16)))
+        kernels.check_device_status(dev)
+        results["raw"] = ok
+        # 2. fused verify forward of a split target: peer exchange == NCCL all-gather
+        headsplit.register()
+        cfg = qwen3_config("small", hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                           num_attention_heads=8, num_key_value_heads=2, vocab_size=1000)
+        model = build_target(cfg, device=dev, seed=5, attn_implementation=headsplit.NAME)
+        headsplit.shard_attention_heads(model, r, world)
+        parents = synthetic.random_tree_parents(9, 32).tolist()
+        n = len(parents)
+        bits = torch.from_numpy(ot.pack_bits(ot.visibility(parents)).view(np.int32)).to(dev)
+        tok = torch.randint(0, 1000, (n,), device=dev, generator=torch.Generator(device=dev).manual_seed(2))
+        pos = torch.arange(300, 300 + n, device=dev)
+        logits = {}
+        with torch.inference_mode():
+            for mode in ("nccl", "p2p"):
+                cache = TreeKVCache(2, 1, 128, 512, device=dev)
+                cache.slab.copy_(torch.randn(cache.slab.shape, device=dev,
+                                             generator=torch.Generator(device=dev).manual_seed(7 + r))
+                                 .to(torch.bfloat16))
+                ft = fused.FusedTarget(model, cache, n_max=64, gemm="cublas", exchange=mode)
+                if ft.peer is not None:
+                    ex.append(ft.peer)
+                logits[mode] = [ft.forward(tok, pos, bits, offset=300).clone() for _ in range(2)]
+        kernels.check_device_status(dev)
+        results["fused"] = all(torch.equal(a, b) for a, b in zip(logits["nccl"], logits["p2p"]))
+        q.put((r, results))
+    except Exception:
+        q.put((r, "ERROR " + traceback.format_exc()))
+    finally:
+        import torch.distributed as dist
+        try:
+            for pe in ex:
+                pe.close()
+        except Exception:
+            pass
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def test_peer_exchange_on_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=600) for _ in procs)
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(2):
+        assert not isinstance(res[r], str), res[r]
+        assert res[r]["raw"], r
+        assert res[r]["fused"], r
