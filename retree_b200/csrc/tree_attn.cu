@@ -665,6 +665,8 @@ __global__ void __launch_bounds__(128) tree_attn_simt_kernel(const AttnParams p)
 // ---------------------------------------------------------------------------
 // Split merge: one warp per (kv head, tile row); lane owns 4 dims.
 // ---------------------------------------------------------------------------
+constexpr int kFastSplits = 24;  // up to this many splits: every load of a row issued at once
+
 __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
   pdl_launch_dependents();
   pdl_wait();
@@ -676,8 +678,48 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
   const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
   const int S = p.num_splits;
   auto slot = [&](int s) { return (static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R; };
-  // lane s holds split s's (max, sum); one load per lane instead of a serial walk
   const float2 none = make_float2(-INFINITY, 0.f);
+  const int node = R / p.group, h = kvh * p.group + (R - node * p.group);
+  if (S <= kFastSplits) {
+    // Every load of the row is independent of the others, so all of them --
+    // the splits' partial rows and (max, sum) pairs -- go out at once: one
+    // L2 round trip instead of one for the maxima and one per batch of rows.
+    // A split whose weight is zero (max -inf) is skipped, never multiplied.
+    float4 o[kFastSplits];
+#pragma unroll
+    for (int u = 0; u < kFastSplits; ++u)
+      o[u] = u < S ? *reinterpret_cast<const float4*>(p.ws_o + slot(u) * kHD + lane * 4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float2 ml = lane < S ? p.ws_ml[slot(lane)] : none;
+    float M = ml.x;
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, off));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lsum = 0.f;
+    if (M > -INFINITY) {
+      const float w = ml.x == -INFINITY ? 0.f : ex2(ml.x - M);
+      lsum = w * ml.y;
+#pragma unroll
+      for (int u = 0; u < kFastSplits; ++u) {
+        const float wu = __shfl_sync(0xFFFFFFFFu, w, u);
+        if (u < S && wu != 0.f) {
+          acc.x = fmaf(wu, o[u].x, acc.x);
+          acc.y = fmaf(wu, o[u].y, acc.y);
+          acc.z = fmaf(wu, o[u].z, acc.z);
+          acc.w = fmaf(wu, o[u].w, acc.w);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, off);
+    }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    uint2 pk;
+    pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+    pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(p.out + node * p.out_tok_stride + h * p.out_head_stride + lane * 8) = pk;
+    return;
+  }
+  // lane s holds split s's (max, sum); one load per lane instead of a serial walk
   const float2 first = lane < S ? p.ws_ml[slot(lane)] : none;
   float M = first.x;
   for (int base = 32; base < S; base += 32) M = fmaxf(M, base + lane < S ? p.ws_ml[slot(base + lane)].x : -INFINITY);
@@ -714,7 +756,6 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
     for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, o);
   }
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-  const int node = R / p.group, h = kvh * p.group + (R - node * p.group);
   uint2 pk;
   pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
   pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
