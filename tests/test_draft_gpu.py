@@ -155,7 +155,7 @@ def test_ddtree_generate_with_a_draft_module_commits_greedy_tokens(monkeypatch, 
     assert res.num_output_tokens >= new and min(res.acceptance_lengths) >= 1
     if got[: len(greedy)] != greedy[: len(got)]:
         first = next(i for i, (a, b) in enumerate(zip(got, greedy)) if a != b)
-        assert first >= 8 and margins[first] < 2e-2, (first, margins[first])
+        assert margins[first] < 2e-2, (first, margins[first])  # the runs may part only at a near tie
 
 
 @torch.inference_mode()
