@@ -670,31 +670,33 @@ constexpr int kFastSplits = 24;  // up to this many splits: every load of a row 
 __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
   pdl_launch_dependents();
   pdl_wait();
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int rows = p.n * p.group;
-  if (gw >= p.num_kv_heads * rows) return;
-  const int kvh = gw / rows, R = gw - kvh * rows;
   const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
   const int S = p.num_splits;
-  auto slot = [&](int s) { return (static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R; };
   const float2 none = make_float2(-INFINITY, 0.f);
-  const int node = R / p.group, h = kvh * p.group + (R - node * p.group);
   if (S <= kFastSplits) {
+    // Two warps per (kv head, row), one per 64-dim half, lane owns 2 dims.
     // Every load of the row is independent of the others, so all of them --
     // the splits' partial rows and (max, sum) pairs -- go out at once: one
     // L2 round trip instead of one for the maxima and one per batch of rows.
-    // A split whose weight is zero (max -inf) is skipped, never multiplied.
-    float4 o[kFastSplits];
+    // A split whose weight is zero (max -inf) is skipped, never multiplied;
+    // the per-element sum runs over the splits in order, as below.
+    const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (gw >= 2 * p.num_kv_heads * rows) return;
+    const int half = gw & 1, pair = gw >> 1;
+    const int kvh = pair / rows, R = pair - kvh * rows;
+    auto slot = [&](int s) { return (static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R; };
+    const int d0 = half * 64 + lane * 2;
+    float2 o[kFastSplits];
 #pragma unroll
     for (int u = 0; u < kFastSplits; ++u)
-      o[u] = u < S ? *reinterpret_cast<const float4*>(p.ws_o + slot(u) * kHD + lane * 4)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+      o[u] = u < S ? *reinterpret_cast<const float2*>(p.ws_o + slot(u) * kHD + d0) : make_float2(0.f, 0.f);
     const float2 ml = lane < S ? p.ws_ml[slot(lane)] : none;
     float M = ml.x;
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xFFFFFFFFu, M, off));
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 acc = make_float2(0.f, 0.f);
     float lsum = 0.f;
     if (M > -INFINITY) {
       const float w = ml.x == -INFINITY ? 0.f : ex2(ml.x - M);
@@ -705,20 +707,21 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
         if (u < S && wu != 0.f) {
           acc.x = fmaf(wu, o[u].x, acc.x);
           acc.y = fmaf(wu, o[u].y, acc.y);
-          acc.z = fmaf(wu, o[u].z, acc.z);
-          acc.w = fmaf(wu, o[u].w, acc.w);
         }
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, off);
     }
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-    uint2 pk;
-    pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
-    pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
-    *reinterpret_cast<uint2*>(p.out + node * p.out_tok_stride + h * p.out_head_stride + lane * 8) = pk;
+    const int node = R / p.group, h = kvh * p.group + (R - node * p.group);
+    *reinterpret_cast<uint32_t*>(p.out + node * p.out_tok_stride + h * p.out_head_stride + d0 * 2) =
+        pack_bf16x2(acc.x * inv, acc.y * inv);
     return;
   }
+  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  if (gw >= p.num_kv_heads * rows) return;
+  const int kvh = gw / rows, R = gw - kvh * rows;
+  auto slot = [&](int s) { return (static_cast<int64_t>(s) * p.num_kv_heads + kvh) * rows_ws + R; };
   // lane s holds split s's (max, sum); one load per lane instead of a serial walk
   const float2 first = lane < S ? p.ws_ml[slot(lane)] : none;
   float M = first.x;
@@ -756,6 +759,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const AttnParams p) {
     for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xFFFFFFFFu, lsum, o);
   }
   const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+  const int node = R / p.group, h = kvh * p.group + (R - node * p.group);
   uint2 pk;
   pk.x = pack_bf16x2(acc.x * inv, acc.y * inv);
   pk.y = pack_bf16x2(acc.z * inv, acc.w * inv);
@@ -912,7 +916,8 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
     if (rc != RT_OK) return rc;
   }
   if (num_splits == 1) return RT_OK;
-  const int warps = num_kv_heads * n * G;
+  // two warps per output row on the combine's fast path (up to kFastSplits splits), one otherwise
+  const int warps = num_kv_heads * n * G * (num_splits <= kFastSplits ? 2 : 1);
   return record_cuda(launch_ex(attn_combine_kernel, dim3((warps + 3) / 4), dim3(128), 0, s, 1, p));
 }
 
