@@ -23,7 +23,8 @@
 // warp-level path (fewer rows): one warp per query row set, shuffle-reduced
 // dot products and online softmax; same partial format.
 //
-// Splits are merged by attn_combine_kernel (one warp per output row).
+// Splits are merged by attn_combine_kernel (two warps per output row up to
+// kFastSplits splits, all loads of a row in flight at once; one warp beyond).
 #include <cuda.h>
 #include <cuda_fp16.h>
 
