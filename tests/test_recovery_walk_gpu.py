@@ -6,7 +6,6 @@ import numpy as np
 import pytest
 import torch
 
-from oracle import tree as ot
 from retree_b200 import kernels
 from retree_b200.recovery import RecoveryMemory
 from retree_b200.recovery_device import DeviceRecoveryMemory
