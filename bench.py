@@ -82,7 +82,7 @@ def parse():
                     help="MB of the following projections' weights each attention launch warms in L2")
     ap.add_argument("--l2-stream", action="store_true",
                     help="warm the next projection's weights in L2 from a side stream next to each launch")
-    ap.add_argument("--exchange", choices=("nccl", "p2p"), default="nccl",
+    ap.add_argument("--exchange", choices=("nccl", "p2p", "p2p_fused"), default="nccl",
                     help="split workloads: attention-output all-gather over NCCL or over peer memory")
     return ap.parse_args()
 
@@ -461,7 +461,7 @@ def run_ours(args, wl, rank, world, local_rank):
                    "projections": projections,
                    "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "
-                                   f"{'peer memory' if args.exchange == 'p2p' else 'NCCL'})"
+                                   f"{dict(nccl='NCCL', p2p='peer memory', p2p_fused='peer memory, pulled by o_proj')[args.exchange]})"
                                    if wl.get("split") else f"dp{world} (one request per GPU)" + (
                                        ", recovery-delta all-gather per step" if world > 1 else "")),
                    "l2": "inputs > L2 (8 GB of weights and the KV cache stream every round)",

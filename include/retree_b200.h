@@ -448,6 +448,22 @@ int rt_linear_plan(int m, int n_out, int k, int epilogue, int* splits, int* stag
 int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* w, int n_out, int epilogue, void* out,
               int64_t ld_out, const rt_qkv_epilogue* qkv, int* status, rt_stream_t stream);
 
+/* ------------------------------------------------------------------------
+ * rt_linear (RT_EPI_STORE) whose X is gathered from the ranks of a KV-head
+ * split as the K loop reaches it: rank r's columns [r*cols_per_rank,
+ * (r+1)*cols_per_rank) of X are rows of x_ranks[r] (row stride ld_x
+ * elements; peer memory for the other ranks, read with plain TMA loads), and
+ * each CTA waits (bounded; RT_DEV_WAIT_TIMEOUT in *status) until
+ * flags_local[r] >= *epoch_dev + epoch_add before its first load from rank r
+ * -- the announcement rt_peer_signal makes.  Replaces the all-gather + o_proj
+ * pair of the split with one launch whose transfers overlap the weight
+ * stream.  cols_per_rank is a multiple of 64, k == world * cols_per_rank,
+ * world <= 8; results equal rt_linear's on the gathered X.
+ * ---------------------------------------------------------------------- */
+int rt_linear_gather(const void* const* x_ranks, int world, int cols_per_rank, int64_t ld_x, int m, const void* w,
+                     int n_out, int k, void* out, int64_t ld_out, const int64_t* flags_local, const int64_t* epoch_dev,
+                     int64_t epoch_add, int* status, rt_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -61,7 +61,41 @@ struct LinearParams {
   int64_t ld_out;
   rt_qkv_epilogue qkv;
   int* status;
+  // gathered X (rt_linear_gather): K block kb lives on rank kb / g_blocks,
+  // announced by g_flags[rank] reaching *g_epoch + g_epoch_add
+  int g_blocks;
+  const int64_t* g_flags;
+  const int64_t* g_epoch;
+  int64_t g_epoch_add;
 };
+
+// X sources of rt_linear_gather: one tensor map per rank's column block
+// (peer memory for the other ranks; plain, non-multicast TMA loads).
+constexpr int kMaxGather = 8;
+struct XSources {
+  CUtensorMap map[kMaxGather];
+};
+
+constexpr uint32_t kPeerWaitLimit = 1u << 22;  // polls x ~64 ns
+
+// Bounded wait for a peer's announcement; on success the async proxy (TMA)
+// is ordered after the acquire.
+__device__ __forceinline__ bool wait_peer_flag(const int64_t* flag, int64_t epoch, volatile int* abort,
+                                               int* status) {
+  for (uint32_t i = 0; i < kPeerWaitLimit; ++i) {
+    int64_t v;
+    asm volatile("ld.acquire.sys.global.s64 %0, [%1];" : "=l"(v) : "l"(flag) : "memory");
+    if (v >= epoch) {
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      return true;
+    }
+    if ((i & 255u) == 255u && *abort) return false;
+    __nanosleep(64);
+  }
+  *abort = 1;
+  set_status(status, RT_DEV_WAIT_TIMEOUT);
+  return false;
+}
 
 struct LinBars {
   uint64_t full[kMaxStages], empty[kMaxStages], acc;
@@ -71,8 +105,10 @@ struct LinBars {
 
 constexpr uint32_t kPartBytes = 32 * 128 * 4;  // one 32-token fp32 partial slice (split-K exchange)
 
+template <bool kGather>
 __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                              const __grid_constant__ CUtensorMap tmap_x,
+                                                             const __grid_constant__ XSources xs,
                                                              const LinearParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -124,28 +160,46 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
           }
         }
       };
-      auto load_x = [&](int it) {
+      uint32_t ready = 0;  // gathered X: ranks whose rows this CTA has seen announced
+      int64_t epoch = 0;
+      auto load_x = [&](int it) -> bool {
         const int s = it % p.stages;
-        unsigned char* xs = smem + s * p.stage_bytes + p.bps * kWTileBytes;
+        unsigned char* xst = smem + s * p.stage_bytes + p.bps * kWTileBytes;
         for (int b = 0; b < p.bps; ++b) {
           const int kx = ((kb0 + it) * p.bps + b) * kBK;
-          for (int c = 0; c < p.chunks; ++c)
-            tma_load_2d(xs + (b * p.chunks + c) * p.chunk_rows * 128, &tmap_x, &bar.full[s], kx, c * p.chunk_rows);
+          if constexpr (kGather) {
+            const int src = (kx / kBK) / p.g_blocks;
+            if (!(ready & (1u << src))) {
+              if (!wait_peer_flag(p.g_flags + src, epoch, abort_flag, p.status)) return false;
+              ready |= 1u << src;
+            }
+            const int lx = kx - src * p.g_blocks * kBK;
+            for (int c = 0; c < p.chunks; ++c)
+              tma_load_2d(xst + (b * p.chunks + c) * p.chunk_rows * 128, &xs.map[src], &bar.full[s], lx,
+                          c * p.chunk_rows);
+          } else {
+            for (int c = 0; c < p.chunks; ++c)
+              tma_load_2d(xst + (b * p.chunks + c) * p.chunk_rows * 128, &tmap_x, &bar.full[s], kx,
+                          c * p.chunk_rows);
+          }
         }
+        return true;
       };
       // the first pass over the ring needs no free slot: weights first, then X
       // once the kernel that writes it has finished
       const int pre = min(nk, p.stages);
       for (int it = 0; it < pre; ++it) load_w(it);
       pdl_wait();
-      for (int it = 0; it < pre; ++it) load_x(it);
+      if constexpr (kGather) epoch = *p.g_epoch + p.g_epoch_add;
       int issued = pre;
-      for (int it = pre; it < nk; ++it) {
+      for (int it = 0; it < pre; ++it)
+        if (!load_x(it)) break;
+      for (int it = pre; it < nk && !(kGather && *abort_flag); ++it) {
         const int s = it % p.stages;
         if (!mbar_wait(&bar.empty[s], ((it / p.stages) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
         load_w(it);
-        load_x(it);
         issued = it + 1;
+        if (!load_x(it)) break;
       }
       if (*abort_flag) {
         // let the copies still in flight land before the block's memory goes away
@@ -351,7 +405,7 @@ int max_active_clusters(int cluster, size_t smem, int tiles) {
   const auto key = std::make_pair(cluster, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  set_smem_limit(linear_kernel, smem);
+  set_smem_limit(linear_kernel<false>, smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, cluster);
   cfg.blockDim = dim3(kLinThreads);
@@ -364,7 +418,7 @@ int max_active_clusters(int cluster, size_t smem, int tiles) {
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, linear_kernel, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, linear_kernel<false>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = 0;
   }
@@ -491,7 +545,57 @@ extern "C" int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* 
   p.ld_out = ld_out;
   if (qkv) p.qkv = *qkv;
   p.status = status;
-  set_smem_limit(linear_kernel, pl.smem);
-  return record_cuda(launch_ex(linear_kernel, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
-                               static_cast<cudaStream_t>(stream), pl.splits, tw, tx, p));
+  set_smem_limit(linear_kernel<false>, pl.smem);
+  static const XSources no_sources{};
+  return record_cuda(launch_ex(linear_kernel<false>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
+                               static_cast<cudaStream_t>(stream), pl.splits, tw, tx, no_sources, p));
+}
+
+extern "C" int rt_linear_gather(const void* const* x_ranks, int world, int cols_per_rank, int64_t ld_x, int m,
+                                const void* w, int n_out, int k, void* out, int64_t ld_out,
+                                const int64_t* flags_local, const int64_t* epoch_dev, int64_t epoch_add, int* status,
+                                rt_stream_t stream) {
+  if (x_ranks == nullptr || world < 1 || world > kMaxGather || cols_per_rank <= 0 || cols_per_rank % kBK ||
+      k != world * cols_per_rank || ld_x < cols_per_rank || (ld_x * 2) % 16 || flags_local == nullptr ||
+      epoch_dev == nullptr)
+    return RT_ERR_INVALID_ARGUMENT;
+  Plan pl;
+  int rc = make_plan(m, n_out, k, RT_EPI_STORE, &pl, true);
+  if (rc != RT_OK) return rc;
+  if (!w || !al16(w) || !out || !al16(out) || ld_out < n_out || (ld_out * 2) % 16) return RT_ERR_INVALID_ARGUMENT;
+  for (int r = 0; r < world; ++r)
+    if (x_ranks[r] == nullptr || !al16(x_ranks[r])) return RT_ERR_INVALID_ARGUMENT;
+  CUtensorMap tw;
+  rc = make_bf16_2d_tmap(&tw, w, n_out, k, k, 128);
+  if (rc != RT_OK) return rc;
+  XSources xs{};
+  for (int r = 0; r < world; ++r) {
+    rc = make_bf16_2d_tmap(&xs.map[r], x_ranks[r], m, cols_per_rank, ld_x, static_cast<uint32_t>(pl.chunk_rows));
+    if (rc != RT_OK) return rc;
+  }
+  LinearParams p{};
+  p.m = m;
+  p.n_out = n_out;
+  p.k = k;
+  p.chunks = pl.chunks;
+  p.chunk_rows = pl.chunk_rows;
+  p.kblocks = pl.kblocks;
+  p.splits = pl.splits;
+  p.per = pl.per;
+  p.tiles = pl.tiles;
+  p.epi = RT_EPI_STORE;
+  p.stages = pl.stages;
+  p.stage_bytes = pl.stage_bytes;
+  p.bps = pl.bps;
+  p.tmem_cols = pl.tmem_cols;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ld_out = ld_out;
+  p.status = status;
+  p.g_blocks = cols_per_rank / kBK;
+  p.g_flags = flags_local;
+  p.g_epoch = epoch_dev;
+  p.g_epoch_add = epoch_add;
+  set_smem_limit(linear_kernel<true>, pl.smem);
+  return record_cuda(launch_ex(linear_kernel<true>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
+                               static_cast<cudaStream_t>(stream), pl.splits, tw, xs.map[0], xs, p));
 }

@@ -218,12 +218,14 @@ class FusedTarget:
                           "gate_up": [(L.down_w, min(nb(L.down_w), cap))],
                           "down": [(nxt, min(nb(nxt), cap))]}
         # under a KV-head split: the attention outputs' all-gather before o_proj,
-        # NCCL ("nccl") or this package's peer-memory exchange ("p2p", retree_b200.peer)
-        if exchange not in ("nccl", "p2p"):
-            raise ValueError("exchange must be 'nccl' or 'p2p'")
+        # NCCL ("nccl"), this package's peer-memory exchange ("p2p", retree_b200.peer),
+        # or that exchange pulled by the o_proj kernel itself ("p2p_fused")
+        if exchange not in ("nccl", "p2p", "p2p_fused"):
+            raise ValueError("exchange must be 'nccl', 'p2p' or 'p2p_fused'")
+        self.exchange = exchange
         self.peer = None
         split = self.layers[0].split
-        if exchange == "p2p" and split is not None and split[1] > 1:
+        if exchange != "nccl" and split is not None and split[1] > 1:
             from .peer import PeerExchange
             if len(self.layers) % 2:
                 raise RuntimeError("the peer exchange alternates two slots by layer: it needs an even layer count")
@@ -416,14 +418,21 @@ class FusedTarget:
                                        scale=L.scale, out=attn_out, num_splits=splits, kv_capacity=cap,
                                        l2_prefetch=L.l2pf)
             attn = attn_out
+            fused_pull = False
             if self.peer is not None:
                 self.peer.signal(L.index)
-                attn = self.peer.gather(L.index, n, self.attn_full[:n])
+                fused_pull = (self.exchange == "p2p_fused" and L.o_b is None
+                              and kernels.linear_supported(n, L.o_w.shape[0], L.o_w.shape[1], 0))
+                if not fused_pull:
+                    attn = self.peer.gather(L.index, n, self.attn_full[:n])
             elif L.split is not None:
                 group, world, _ = L.split
                 attn = gather_heads(attn.unsqueeze(0), group, world)[0]
             warm(L, "o")
-            self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n], kind="o")
+            if fused_pull:
+                self.peer.linear(L.index, n, L.o_w, self.o[:n])
+            else:
+                self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n], kind="o")
             kernels.add_rmsnorm(self.o[:n], res, L.post_norm, L.eps_post, xn)
             warm(L, "gate_up")
             self._linear(xn, L.gate_up_w, None, self.act[:n], epilogue=1, kind="gate_up")

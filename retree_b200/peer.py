@@ -11,7 +11,11 @@ once through the process group; plain peer mappings, no multicast object):
                      array (rt_peer_signal);
   ``gather(layer)``  waits (bounded, per source rank) for the flags and copies
                      every rank's rows into the ``[n, world * cols]`` o_proj
-                     input (rt_peer_gather).
+                     input (rt_peer_gather);
+  ``linear(layer)``  or, instead of gather + o_proj, the o_proj itself pulls
+                     each rank's columns as its K loop reaches them, after the
+                     same wait (rt_linear_gather), so the transfers overlap the
+                     weight stream.
 
 Two slots alternate by layer, which is safe without a consumed-handshake: rank
 r writes a slot again two layers later, after its own o_proj of the layer in
@@ -125,6 +129,23 @@ class PeerExchange:
             self._slot_ptrs[layer % 2], self.world, rows, self.cols * 2, self.cols * 2, out.data_ptr(),
             out.stride(0) * 2, self.flags_local.data_ptr(), self.epoch.data_ptr(), self._epoch_add(layer),
             kernels.status_tensor(self.device).data_ptr(), kernels._stream(self.device)), "rt_peer_gather")
+        kernels._count()
+        return out
+
+    def linear(self, layer: int, rows: int, w: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """``out [rows, n_out] = X @ w^T`` with X gathered from every rank's slot inside the projection
+        (rt_linear_gather: each CTA waits for a rank's announcement before its first load of that rank's
+        columns; no separate gather launch)."""
+        n_out, k = w.shape
+        if k != self.world * self.cols or w.dtype != torch.bfloat16 or not w.is_contiguous():
+            raise RuntimeError("weights must be contiguous bf16 [n_out, world * cols]")
+        if out.dtype != torch.bfloat16 or out.stride(-1) != 1 or out.shape[-1] != n_out:
+            raise RuntimeError("out must be bf16 [rows, n_out] with unit inner stride")
+        _lib.check(_lib.load().rt_linear_gather(
+            self._slot_ptrs[layer % 2], self.world, self.cols, self.cols, rows, w.data_ptr(), n_out, k,
+            out.data_ptr(), out.stride(0), self.flags_local.data_ptr(), self.epoch.data_ptr(),
+            self._epoch_add(layer), kernels.status_tensor(self.device).data_ptr(), kernels._stream(self.device)),
+            "rt_linear_gather")
         kernels._count()
         return out
 

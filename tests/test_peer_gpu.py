@@ -4,8 +4,9 @@
 deliver every rank's rows in head order, layer after layer and forward after
 forward (epochs from the device counter, two alternating slots), and the fused
 verify forward of a split target must give the same logits with it as with the
-NCCL all-gather.  NVLS is off (NCCL_NVLS_ENABLE=0); the exchange itself uses
-plain peer mappings.
+NCCL all-gather -- also when o_proj pulls the rows itself (rt_linear_gather,
+compared with rt_linear on the NCCL-gathered rows).  NVLS is off
+(NCCL_NVLS_ENABLE=0); the exchange itself uses plain peer mappings.
 """
 
 import os
@@ -80,17 +81,21 @@ def _worker(r, world, port, q):
         pos = torch.arange(300, 300 + n, device=dev)
         logits = {}
         with torch.inference_mode():
-            for mode in ("nccl", "p2p"):
+            for mode, gemm in (("nccl", "cublas"), ("p2p", "cublas"), ("nccl", "tcgen05"),
+                               ("p2p_fused", "tcgen05")):
                 cache = TreeKVCache(2, 1, 128, 512, device=dev)
                 cache.slab.copy_(torch.randn(cache.slab.shape, device=dev,
                                              generator=torch.Generator(device=dev).manual_seed(7 + r))
                                  .to(torch.bfloat16))
-                ft = fused.FusedTarget(model, cache, n_max=64, gemm="cublas", exchange=mode)
+                ft = fused.FusedTarget(model, cache, n_max=64, gemm=gemm, exchange=mode)
                 if ft.peer is not None:
                     ex.append(ft.peer)
-                logits[mode] = [ft.forward(tok, pos, bits, offset=300).clone() for _ in range(2)]
+                logits[mode, gemm] = [ft.forward(tok, pos, bits, offset=300).clone() for _ in range(2)]
         kernels.check_device_status(dev)
-        results["fused"] = all(torch.equal(a, b) for a, b in zip(logits["nccl"], logits["p2p"]))
+        same = lambda a, b: all(torch.equal(x, y) for x, y in zip(logits[a], logits[b]))  # noqa: E731
+        # the gather kernel then cuBLAS; the o_proj pulling the rows itself (rt_linear_gather) vs rt_linear
+        results["fused"] = same(("nccl", "cublas"), ("p2p", "cublas")) and same(("nccl", "tcgen05"),
+                                                                                ("p2p_fused", "tcgen05"))
         q.put((r, results))
     except Exception:
         q.put((r, "ERROR " + traceback.format_exc()))
