@@ -82,6 +82,10 @@ def parse():
                     help="MB of the following projections' weights each attention launch warms in L2")
     ap.add_argument("--l2-stream", action="store_true",
                     help="warm the next projection's weights in L2 from a side stream next to each launch")
+    ap.add_argument("--dp-exchange", choices=("nccl", "p2p"), default="nccl",
+                    help="request DP at N>1: the per-step recovery-delta all-gather over NCCL or over peer memory")
+    ap.add_argument("--pdl", choices=("auto", "on", "off"), default="auto",
+                    help="programmatic dependent launch (auto: on at N=1, off when NCCL runs beside the kernels)")
     ap.add_argument("--exchange", choices=("nccl", "p2p", "p2p_fused"), default="nccl",
                     help="split workloads: attention-output all-gather over NCCL or over peer memory")
     return ap.parse_args()
@@ -300,10 +304,26 @@ def run_ours(args, wl, rank, world, local_rank):
                               torch.randint(0, cfg.vocab_size, (DELTA_PAIRS,), device=dev, generator=g),
                               torch.randint(1, 5, (DELTA_PAIRS,), device=dev, generator=g)], dim=1).to(torch.int32)
     delta_recv = torch.zeros((world, DELTA_PAIRS, 3), dtype=torch.int32, device=dev) if world > 1 else None
+    delta_peer = None
+    if world > 1 and not wl.get("split") and args.dp_exchange == "p2p":
+        from retree_b200.peer import PeerExchange
+        # one row of DELTA_PAIRS * 3 int32 per rank, carried as bf16 columns; two slots by step parity
+        delta_peer = PeerExchange(None, rank, world, 1, DELTA_PAIRS * 3 * 2, 2, dev)
+    n_exchanges = [0]
 
     def exchange():
-        if world > 1 and not wl.get("split"):
+        if world <= 1 or wl.get("split"):
+            return
+        if delta_peer is None:
             dist.all_gather_into_tensor(delta_recv.view(world * DELTA_PAIRS, 3), delta_send)
+            return
+        slot = n_exchanges[0] % 2
+        if slot == 0:
+            delta_peer.step()
+        delta_peer.slot(slot, 1).view(torch.int32).copy_(delta_send.view(1, -1))
+        delta_peer.signal(slot)
+        delta_peer.gather(slot, 1, delta_recv.view(1, -1).view(torch.bfloat16))
+        n_exchanges[0] += 1
 
     def barrier():
         if world > 1:
@@ -432,6 +452,8 @@ def run_ours(args, wl, rank, world, local_rank):
     for vv in (v, v2):  # peer-memory exchanges unmap on every rank together
         if vv.fused is not None and vv.fused.peer is not None:
             vv.fused.peer.close()
+    if delta_peer is not None:
+        delta_peer.close()
     if rank != 0:
         return
     hbm_peak, tf_peak, peak_kind = measured_peaks()
@@ -448,6 +470,8 @@ def run_ours(args, wl, rank, world, local_rank):
                           f"random-KV prefix of {wl['prompt']} tokens")}
     reqs = 1 if wl.get("split") else world  # a split request is one request over all ranks
     value = reqs * steps / dev_s
+    split_exchange = dict(nccl="NCCL", p2p="peer memory", p2p_fused="peer memory, pulled by o_proj")[args.exchange]
+    dp_exchange = "peer memory" if args.dp_exchange == "p2p" else "NCCL"
     print(json.dumps({
         "metric": "verify rounds/sec", "value": value, "unit": "rounds/s", "n_gpus": world, "steps": steps,
         "warmup": warm, "ms_per_step": 1000.0 * dev_s / steps, "higher_is_better": True,
@@ -461,9 +485,10 @@ def run_ours(args, wl, rank, world, local_rank):
                    "projections": projections,
                    "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "
-                                   f"{dict(nccl='NCCL', p2p='peer memory', p2p_fused='peer memory, pulled by o_proj')[args.exchange]})"
-                                   if wl.get("split") else f"dp{world} (one request per GPU)" + (
-                                       ", recovery-delta all-gather per step" if world > 1 else "")),
+                                   f"{split_exchange})" if wl.get("split") else
+                                   f"dp{world} (one request per GPU)" + (
+                                       f", recovery-delta all-gather per step ({dp_exchange})" if world > 1 else "")),
+                   "pdl": kernels.pdl_enabled(),
                    "l2": "inputs > L2 (8 GB of weights and the KV cache stream every round)",
                    "mean_accepted": sum(accepted) / len(accepted), "wall_s": wall},
         "roofline": {"kernel": "tree_attn (rt_tree_attn + split combine)", "bound": "hbm", "achieved": achieved,
@@ -492,15 +517,19 @@ def main():
         import torch.distributed as dist
         # the per-step exchanges are tiny all-gathers: no NVLink multicast objects needed
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        # no programmatic dependent launch next to NCCL streams (rt_set_pdl), from the first launch on
-        os.environ["RETREE_B200_PDL"] = "0"
+        # no programmatic dependent launch next to NCCL streams (rt_set_pdl), from the first launch on,
+        # unless asked for (--pdl on)
+        os.environ["RETREE_B200_PDL"] = "1" if args.pdl == "on" else "0"
 
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
         from retree_b200 import kernels
-        kernels.set_pdl(False)  # NCCL collectives share the stream with the forward's kernels
+        kernels.set_pdl(args.pdl == "on")  # NCCL collectives share the stream with the forward's kernels
         log(rank, "process group up")
+    elif args.pdl != "auto":
+        from retree_b200 import kernels
+        kernels.set_pdl(args.pdl == "on")
     try:
         run_ours(args, wl, rank, world, local_rank)
     finally:
