@@ -108,14 +108,19 @@ def _device_context(context_ids, device):
 
 
 def build_tree_device(draft_logits: torch.Tensor, budget: int, context_ids=None, strategy: str | None = None,
-                      params: NgramParams | None = None, out: dict | None = None, **kw) -> dict:
-    """Top-k + tree expansion on the device; returns the device tensors of ``kernels.tree_build``."""
+                      params: NgramParams | None = None, out: dict | None = None, k: int | None = None,
+                      **kw) -> dict:
+    """Top-k + tree expansion on the device; returns the device tensors of ``kernels.tree_build``.
+
+    ``k`` candidates per draft row (default min(budget, vocab), the reference's
+    top-k; 1 gives the chain of the rows' argmax tokens).
+    """
     if strategy is None or params is None:
         strategy, params = resolve_strategy()
     if not draft_logits.is_cuda:
         raise RuntimeError("build_ddtree_tree runs on the device: pass CUDA draft logits")
     logits = draft_logits if draft_logits.stride(-1) == 1 else draft_logits.contiguous()
-    k = min(max(int(budget), 1), logits.shape[-1])
+    k = min(max(int(budget), 1) if k is None else max(int(k), 1), logits.shape[-1])
     top_logp, top_ids, _ = kernels.draft_topk(logits, k)
     ctx = _device_context(context_ids, logits.device)
     return kernels.tree_build(top_logp, top_ids, int(budget), strategy, params, ctx=ctx, out=out, **kw)
@@ -312,8 +317,9 @@ def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, 
     """
     from .verify import TreeVerifier
 
-    if block_size <= 1:
-        raise NotImplementedError("block_size <= 1 is the linear DFlash baseline, outside the tree path")
+    if block_size <= 1:  # ddtree.py:747-757: the linear path
+        return dflash_generate(model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
+                               temperature=temperature, draft_fn=draft_fn, fused=fused, fused_draft=fused_draft)
     layer_ids = None if (model is None or draft_fn is not None) else list(model.target_layer_ids)
     verifier = TreeVerifier(target, tree_budget=(block_size - 1) if tree_budget is None else max(tree_budget, 0),
                             max_length=input_ids.shape[1] + max_new_tokens + 2 * block_size + 8,
@@ -321,3 +327,26 @@ def ddtree_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, 
                             fused=fused, fused_draft=fused_draft)
     return verifier.generate(input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
                              draft_model=model, draft_fn=draft_fn, save_tree_traces=save_tree_traces)
+
+
+@torch.inference_mode()
+def dflash_generate(model, target, input_ids: torch.Tensor, mask_token_id: int, max_new_tokens: int,
+                    block_size: int, stop_token_ids, temperature: float = 0.0, draft_fn=None,
+                    fused: bool | None = None, fused_draft: bool = False) -> SimpleNamespace:
+    """The linear DFlash decode loop of dflash.py:14-162 on the device kernels.
+
+    Each round verifies the chain of the draft rows' argmax tokens (a tree with
+    one candidate per row; the exact walk accepts its longest matching
+    prefix, dflash.py:108-118); ``block_size <= 1`` decodes one target token
+    per round without a draft.  Arguments as in ``ddtree_generate``.
+    """
+    from .verify import TreeVerifier
+
+    chain = max(int(block_size) - 1, 0)
+    layer_ids = None if (chain == 0 or model is None or draft_fn is not None) else list(model.target_layer_ids)
+    verifier = TreeVerifier(target, tree_budget=chain,
+                            max_length=input_ids.shape[1] + max_new_tokens + 2 * max(block_size, 1) + 8,
+                            draft_horizon=max(chain, 1), temperature=temperature, target_layer_ids=layer_ids,
+                            fused=fused, fused_draft=fused_draft, chain=True)
+    return verifier.generate(input_ids, mask_token_id, max_new_tokens, max(int(block_size), 1), stop_token_ids,
+                             draft_model=model, draft_fn=draft_fn)

@@ -99,8 +99,12 @@ def retree_generate(model, target, input_ids, mask_token_id, max_new_tokens, blo
     """
     from .verify import TreeVerifier
 
-    if block_size <= 1:
-        raise NotImplementedError("block_size <= 1 is the linear DFlash baseline, outside the tree path")
+    if block_size <= 1:  # retree.py:210-219: the linear path
+        from .ddtree import dflash_generate
+        out = dflash_generate(model, target, input_ids, mask_token_id, max_new_tokens, block_size, stop_token_ids,
+                              temperature=temperature, draft_fn=draft_fn, fused=fused, fused_draft=fused_draft)
+        out.total_rescued = 0
+        return out
     stop_set = None if stop_token_ids is None else {int(t) for t in stop_token_ids if t is not None}
     rescued = [0]
 

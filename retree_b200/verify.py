@@ -37,9 +37,10 @@ from .ddtree import (DDTREE_STAGE_ORDER, DDTREE_TREE_BUILD_STAGE_ORDER, build_tr
                      empty_stage_times, resolve_strategy, sample)
 
 
-def expected_tree_size(budget: int, rows: int, vocab: int) -> int:
-    """Nodes the best-first expansion emits: ``budget`` unless the tree runs out of candidates."""
-    k = min(max(budget, 1), vocab)
+def expected_tree_size(budget: int, rows: int, vocab: int, k: int | None = None) -> int:
+    """Nodes the best-first expansion emits: ``budget`` unless the tree runs out of candidates
+    (``k`` candidates per draft row; default min(budget, vocab))."""
+    k = min(max(budget, 1), vocab) if k is None else min(k, vocab)
     total, level = 0, 1
     for _ in range(rows):
         level *= k
@@ -58,7 +59,7 @@ class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
                  temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None,
                  gemm: str = "auto", fused_draft: bool = False, attn_l2_prefetch: int | None = None,
-                 l2_stream: bool | None = None, exchange: str = "nccl"):
+                 l2_stream: bool | None = None, exchange: str = "nccl", chain: bool = False):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -108,6 +109,11 @@ class TreeVerifier:
         self.timed = False
         self.debug = False  # keep the posterior and the pre-compaction cache of the last round
         self.strategy, self.params = resolve_strategy()
+        # chain mode (the linear DFlash baseline, dflash.py:73-118): one candidate per
+        # draft row, so the best-first expansion is the chain of the rows' argmax tokens
+        self.topk = 1 if chain else None
+        if chain:
+            self.strategy = "heap"
         # verify forward: fused stages (retree_b200.fused) unless the model is not
         # one they cover; with target_layer_ids the fused forward also writes the
         # selected layer outputs (the draft's context features)
@@ -224,7 +230,7 @@ class TreeVerifier:
         """One round with every varying quantity on the device (capturable)."""
         n = 1 + count
         if self.budget > 0:
-            build_tree_device(logits, self.budget, self.output_ids, self.strategy, self.params, out=self.tree,
+            build_tree_device(logits, self.budget, self.output_ids, self.strategy, self.params, out=self.tree, k=self.topk,
                               ctx_len=1, ctx_len_dev=self.start_dev[:1], start_dev=self.start_dev[:1])
         else:
             raise RuntimeError("graph mode needs a tree budget > 0")
@@ -244,7 +250,7 @@ class TreeVerifier:
 
     def _graph_round(self, draft_logits: torch.Tensor) -> int:
         rows, vocab = draft_logits.shape
-        count = expected_tree_size(self.budget, rows, vocab)
+        count = expected_tree_size(self.budget, rows, vocab, self.topk)
         if self.start + self.n_max + 1 > self.output_ids.numel():
             raise RuntimeError("TreeVerifier max_length exceeded")
         if self.graph is None:
@@ -290,12 +296,12 @@ class TreeVerifier:
             raise RuntimeError("TreeVerifier max_length exceeded")
         t = cuda_time() if self.timed else 0.0
         rows, vocab = draft_logits.shape
-        count = expected_tree_size(self.budget, rows, vocab) if self.budget > 0 else 0
+        count = expected_tree_size(self.budget, rows, vocab, self.topk) if self.budget > 0 else 0
         n = 1 + count
         # 1. tree (context = committed ids up to and including the root)
         if self.budget > 0:
             build_tree_device(draft_logits, self.budget, self.output_ids, self.strategy, self.params,
-                              out=self.tree, ctx_len=start + 1, start=start)
+                              out=self.tree, ctx_len=start + 1, start=start, k=self.topk)
         else:
             self.tree["verify_ids"][0] = self.output_ids[start]
             self.tree["verify_pos"][0] = start
@@ -398,7 +404,10 @@ class TreeVerifier:
         r = 0
         while self.start < max_length:
             ts = cuda_time()
-            logits = self._draft(draft_model, draft_fn, r, block_size)
+            if self.budget == 0:  # no draft: one target token per round (dflash.py with block_size <= 1)
+                logits = torch.empty((0, self.target.config.vocab_size), dtype=torch.bfloat16, device=self.device)
+            else:
+                logits = self._draft(draft_model, draft_fn, r, block_size)
             if r > 0:
                 self.stage_times["draft"] += cuda_time() - ts
             else:

@@ -176,3 +176,43 @@ def test_attention_backend_runs_the_draft_attention_non_causal():
                                          v.float().repeat_interleave(4, 1), scale=128 ** -0.5)
     err = (out[0].float() - ref[0].transpose(0, 1)).abs()
     assert float(err.max()) < 2e-2 and float(err.mean()) < 1e-3
+
+
+@torch.inference_mode()
+@pytest.mark.parametrize("block_size", [1, 16])
+def test_linear_dflash_loop_commits_greedy_tokens(monkeypatch, block_size):
+    """dflash_generate (the linear baseline; block_size <= 1: no draft) commits the target's greedy tokens,
+    and ddtree_generate / retree_generate hand block_size <= 1 to it as the reference does."""
+    from retree_b200.ddtree import dflash_generate
+    from retree_b200.retree import retree_generate
+
+    dev = cuda()
+    target = _target(512, 2, dev, seed=10)
+    prompt = torch.from_numpy(synthetic.context_ids(6, 48, VOCAB, alphabet=30))[None].to(dev)
+    new = 24
+    cache = TreeKVCache.for_model(target.config, capacity=256, device=dev)
+    out = target(prompt, position_ids=torch.arange(48, device=dev)[None], past_key_values=cache, use_cache=True)
+    greedy, margins = [int(out.logits[0, -1].argmax())], [1.0]
+    for i in range(new - 1):
+        o = target(torch.tensor([[greedy[-1]]], device=dev), position_ids=torch.tensor([[48 + i]], device=dev),
+                   past_key_values=cache, use_cache=True)
+        top2 = o.logits[0, -1].float().topk(2).values
+        margins.append(float(top2[0] - top2[1]) / max(float(top2[0].abs()), 1.0))
+        greedy.append(int(o.logits[0, -1].argmax()))
+
+    def draft_fn(output_ids, start, r):
+        return torch.randn((15, VOCAB), device=dev, generator=torch.Generator(device=dev).manual_seed(r))
+
+    runs = [dflash_generate(None, target, prompt, VOCAB - 1, new, block_size, None, draft_fn=draft_fn)]
+    if block_size == 1:
+        runs.append(ddtree_generate(None, target, prompt, VOCAB - 1, new, block_size, None))
+        runs.append(retree_generate(None, target, prompt, VOCAB - 1, new, block_size, None))
+    kernels.check_device_status(dev)
+    for res in runs:
+        got = res.output_ids[0, 48:].tolist()
+        assert res.num_output_tokens >= new
+        if block_size == 1:
+            assert set(res.acceptance_lengths) == {1}
+        if got[: len(greedy)] != greedy[: len(got)]:
+            first = next(i for i, (a, b) in enumerate(zip(got, greedy)) if a != b)
+            assert margins[first] < 2e-2, (first, margins[first])

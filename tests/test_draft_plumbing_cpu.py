@@ -249,3 +249,13 @@ def test_attention_backend_honours_is_causal_without_a_mask(fake_kernels, module
     ref = F.scaled_dot_product_attention(q.float(), k.float().repeat_interleave(2, 1),
                                          v.float().repeat_interleave(2, 1), attn_mask=mask, scale=128 ** -0.5)
     assert float((out[0].float() - ref[0].transpose(0, 1)).abs().max()) < 2e-2
+
+
+def test_chain_tree_size_is_one_node_per_draft_row():
+    """The linear baseline's tree (one candidate per row) has min(budget, rows) nodes."""
+    from retree_b200.verify import expected_tree_size
+
+    assert expected_tree_size(15, 15, 151936, k=1) == 15
+    assert expected_tree_size(15, 7, 151936, k=1) == 7
+    assert expected_tree_size(0, 7, 151936, k=1) == 0
+    assert expected_tree_size(16, 15, 151936) == 16  # the reference's top-k: budget candidates per row
