@@ -141,3 +141,33 @@ def test_peer_exchange_argument_checks_without_gpu():
     assert lib.rt_ipc_alloc(0, ctypes.byref(ctypes.c_void_p()), (ctypes.c_ubyte * 64)()) == _lib.RT_ERR_INVALID_ARGUMENT
     assert lib.rt_ipc_open(None, ctypes.byref(ctypes.c_void_p())) == _lib.RT_ERR_INVALID_ARGUMENT
     assert lib.rt_peer_epoch_step(None, 1, None) == _lib.RT_ERR_INVALID_ARGUMENT
+
+
+def test_l2_warm_share_arithmetic_stays_inside_each_range():
+    """The per-CTA share / 32 KB piece arithmetic of l2_warm_share (csrc/common.cuh), emulated: every request
+    lies inside its range, is a multiple of 16 bytes, and together the requests cover the range once."""
+    import random
+
+    def requests(nbytes, ctas, parts, piece=32768):
+        per = (((nbytes + ctas - 1) // ctas) + 15) & ~15
+        out = []
+        for c in range(ctas):
+            b0, b1 = c * per, min(nbytes, c * per + per)
+            for part in range(parts):
+                o = b0 + part * piece
+                while o < b1:
+                    out.append((o, min(piece, b1 - o)))
+                    o += parts * piece
+        return out
+
+    rng = random.Random(0)
+    cases = [(16, 1, 30), (48000, 136, 30), (21 << 20, 136, 30), (100 << 20, 16, 32), (96, 148, 32)]
+    cases += [(16 * rng.randint(1, 1 << 22), rng.randint(1, 300), rng.choice((30, 32))) for _ in range(40)]
+    for nbytes, ctas, parts in cases:
+        reqs = sorted(requests(nbytes, ctas, parts))
+        assert all(o % 16 == 0 and n % 16 == 0 and n > 0 and o + n <= nbytes for o, n in reqs), (nbytes, ctas)
+        pos = 0
+        for o, n in reqs:
+            assert o == pos, (nbytes, ctas, parts)
+            pos += n
+        assert pos == nbytes
