@@ -52,6 +52,7 @@ WORKLOADS = {
     "qwen3-8b-l32k-b256-split": dict(model="qwen3-8b", prompt=32768, budget=256, block=16, split=True),
 }
 DELTA_PAIRS = 4096  # recovery-memory delta exchanged per step at N>1 (int32 draft, target, count)
+RECOVERY_PRIOR_PAIRS = 100_000  # --recovery: size of the seeded recovery-memory prior
 
 
 def prompt_len(wl: dict, req: int) -> int:
@@ -82,6 +83,9 @@ def parse():
                     help="MB of the following projections' weights each attention launch warms in L2")
     ap.add_argument("--l2-stream", action="store_true",
                     help="warm the next projection's weights in L2 from a side stream next to each launch")
+    ap.add_argument("--recovery", action="store_true",
+                    help="walk with ReTree's target-gated sibling recovery on the device (rt_recovery_walk) over a "
+                         "seeded recovery memory, instead of the exact walk")
     ap.add_argument("--dp-exchange", choices=("nccl", "p2p"), default="nccl",
                     help="request DP at N>1: the per-step recovery-delta all-gather over NCCL or over peer memory")
     ap.add_argument("--pdl", choices=("auto", "on", "off"), default="auto",
@@ -296,6 +300,20 @@ def run_ours(args, wl, rank, world, local_rank):
             v.prefill_random(plen, seed=req)
         else:
             v.prefill(prompt.to(dev))
+        if args.recovery:
+            from retree_b200.recovery import RecoveryMemory
+            from retree_b200.recovery_device import DeviceRecoveryMemory
+            # seeded prior: RECOVERY_PRIOR_PAIRS (draft, target) pairs with counts 1..10; a log large
+            # enough for every round of the run between syncs
+            mem = RecoveryMemory(freq_threshold=6)
+            rng = np.random.default_rng(4242 + req)
+            pairs = rng.integers(0, cfg.vocab_size, size=(RECOVERY_PRIOR_PAIRS, 2))
+            counts = rng.integers(1, 11, size=RECOVERY_PRIOR_PAIRS)
+            for (d, t), c in zip(pairs.tolist(), counts.tolist()):
+                mem.record_prior(d, t, c)
+            v.enable_recovery(DeviceRecoveryMemory(mem, dev, capacity=1 << 21, log_capacity=1 << 20),
+                              gate_threshold=0.01,
+                              rescue_top_k=8, record_top_k=8, online_update=True)
         return v
 
     # the step's recovery-memory delta: seeded random (draft, target) pairs and counts
@@ -484,6 +502,7 @@ def run_ours(args, wl, rank, world, local_rank):
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
                    "projections": projections,
                    "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
+                   "walk": "target-gated sibling recovery (device)" if args.recovery else "exact",
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "
                                    f"{split_exchange})" if wl.get("split") else
                                    f"dp{world} (one request per GPU)" + (
