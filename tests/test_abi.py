@@ -171,3 +171,35 @@ def test_l2_warm_share_arithmetic_stays_inside_each_range():
             assert o == pos, (nbytes, ctas, parts)
             pos += n
         assert pos == nbytes
+
+
+def test_a_plain_c_host_compiles_links_and_calls_the_abi(tmp_path):
+    """include/retree_b200.h is C11 (pedantic, warnings as errors), and a C program links the library and
+    calls its host-only entry points (no GPU needed for these)."""
+    import shutil
+    import subprocess
+
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lib = _lib.LIB_PATH
+    assert lib.exists(), "build the library first (python -m retree_b200.build)"
+    src = tmp_path / "host.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include "retree_b200.h"
+int main(void) {
+  rt_l2_ranges r = {0};
+  (void)r;
+  printf("%d %s %zu %d\n", rt_abi_version(), rt_status_string(RT_ERR_INVALID_ARGUMENT),
+         rt_tree_attn_workspace_size(17, 32, 8, 128, 2048, 17), rt_linear_check(17, 2560, 4096, RT_EPI_STORE));
+  return 0;
+}
+""")
+    exe = tmp_path / "host"
+    subprocess.run([gcc, "-std=c11", "-Wall", "-Wextra", "-pedantic", "-Werror", "-I", str(HEADER.parent), str(src),
+                    "-o", str(exe), "-L", str(lib.parent), "-lretree_b200", f"-Wl,-rpath,{lib.parent}"], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()
+    want_ws = _lib.load().rt_tree_attn_workspace_size(17, 32, 8, 128, 2048, 17)
+    assert out[0] == "2" and " ".join(out[1:-2]) == "invalid argument"
+    assert int(out[-2]) == want_ws > 0 and out[-1] == "0"
