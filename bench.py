@@ -83,6 +83,8 @@ def parse():
                     help="MB of the following projections' weights each attention launch warms in L2")
     ap.add_argument("--l2-stream", action="store_true",
                     help="warm the next projection's weights in L2 from a side stream next to each launch")
+    ap.add_argument("--fused-argmax", action="store_true",
+                    help="the lm_head projection also returns the posterior (rt_linear_argmax), no argmax pass")
     ap.add_argument("--recovery", action="store_true",
                     help="walk with ReTree's target-gated sibling recovery on the device (rt_recovery_walk) over a "
                          "seeded recovery memory, instead of the exact walk")
@@ -295,7 +297,7 @@ def run_ours(args, wl, rank, world, local_rank):
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
                          fused=not args.hf_forward, gemm=args.gemm,
                          attn_l2_prefetch=int(args.attn_l2_prefetch * 2**20), l2_stream=args.l2_stream,
-                         exchange=args.exchange)
+                         exchange=args.exchange, fused_argmax=args.fused_argmax)
         if wl.get("split"):
             v.prefill_random(plen, seed=req)
         else:
@@ -503,6 +505,7 @@ def run_ours(args, wl, rank, world, local_rank):
                    "projections": projections,
                    "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
                    "walk": "target-gated sibling recovery (device)" if args.recovery else "exact",
+                   "posterior": "argmax fused into the lm_head projection" if args.fused_argmax else "torch.argmax",
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "
                                    f"{split_exchange})" if wl.get("split") else
                                    f"dp{world} (one request per GPU)" + (

@@ -449,6 +449,17 @@ int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* w, int n_ou
               int64_t ld_out, const rt_qkv_epilogue* qkv, int* status, rt_stream_t stream);
 
 /* ------------------------------------------------------------------------
+ * rt_linear (RT_EPI_STORE) that also returns each token's argmax over the
+ * n_out outputs: index[t] = the first row of the largest bf16 value of out[t]
+ * (NaN counts as the largest, -0.0 equals +0.0) -- sample(logits) at
+ * temperature 0, model/utils.py:52-54, without a second pass over the
+ * [m, n_out] logits.  keys is device scratch of m 8-byte words (zeroed here on
+ * the stream); index is int64[m] on the device.
+ * ---------------------------------------------------------------------- */
+int rt_linear_argmax(const void* x, int64_t ld_x, int m, int k, const void* w, int n_out, void* out, int64_t ld_out,
+                     void* keys, int64_t* index, int* status, rt_stream_t stream);
+
+/* ------------------------------------------------------------------------
  * rt_linear (RT_EPI_STORE) whose X is gathered from the ranks of a KV-head
  * split as the K loop reaches it: rank r's columns [r*cols_per_rank,
  * (r+1)*cols_per_rank) of X are rows of x_ranks[r] (row stride ld_x

@@ -44,6 +44,7 @@ SIGNATURES = {
     "rt_peer_signal": (_I, [_P, _I, _I, _P, _I64, _P]),
     "rt_peer_gather": (_I, [_P, _I, _I, _I64, _I64, _P, _I64, _P, _P, _I64, _P, _P]),
     "rt_linear_gather": (_I, [_P, _I, _I, _I64, _I, _P, _I, _I, _P, _I64, _P, _P, _I64, _P, _P]),
+    "rt_linear_argmax": (_I, [_P, _I64, _I, _I, _P, _I, _P, _I64, _P, _P, _P, _P]),
     "rt_tree_attn_noalloc_max_bytes": (_SZ, []),
     "rt_tree_attn_noalloc": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                                   _I, _I, _I, _F, _I, _I, _P, _P]),

@@ -67,6 +67,8 @@ struct LinearParams {
   const int64_t* g_flags;
   const int64_t* g_epoch;
   int64_t g_epoch_add;
+  // rt_linear_argmax: per token the max of argmax_key over the output row (zeroed before the launch)
+  unsigned long long* am_keys;
 };
 
 // X sources of rt_linear_gather: one tensor map per rank's column block
@@ -105,7 +107,26 @@ struct LinBars {
 
 constexpr uint32_t kPartBytes = 32 * 128 * 4;  // one 32-token fp32 partial slice (split-K exchange)
 
-template <bool kGather>
+// kMode: kPlain, kGatherX (X gathered from the ranks of a split, rt_linear_gather)
+// or kArgmax (store + per-token argmax keys, rt_linear_argmax).
+constexpr int kPlain = 0, kGatherX = 1, kArgmax = 2;
+
+// Order-preserving key of a logit for the argmax: larger value -> larger key,
+// -0.0 == +0.0, NaN above every number (torch.argmax returns a NaN's index);
+// the low half favours the smaller row on equal values.
+__device__ __forceinline__ unsigned long long argmax_key(float x, uint32_t row) {
+  uint32_t b = __float_as_uint(x);
+  uint32_t k;
+  if (x != x) {
+    k = 0xFFFFFFFFu;
+  } else {
+    if (b == 0x80000000u) b = 0u;
+    k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  }
+  return (static_cast<unsigned long long>(k) << 32) | (0xFFFFFFFFu - row);
+}
+
+template <int kMode>
 __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                              const __grid_constant__ CUtensorMap tmap_x,
                                                              const __grid_constant__ XSources xs,
@@ -115,6 +136,7 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   LinBars& bar = *reinterpret_cast<LinBars*>(smem + p.stages * p.stage_bytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr bool kGather = kMode == kGatherX;
   const int tile = blockIdx.x, split = blockIdx.y;
   const int kb0 = split * p.per;
   const int nk = max(0, min(p.kblocks, kb0 + p.per) - kb0);
@@ -323,6 +345,27 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
         const uint4 v = reinterpret_cast<const uint4*>(stile)[t * 16 + c];
         *reinterpret_cast<uint4*>(p.out + t * p.ld_out + tile * 128 + c * 8) = v;
       }
+      if constexpr (kMode == kArgmax) {
+        // one warp per token: the best of the tile's 128 bf16 values (4 a lane), then one
+        // 64-bit atomicMax per (tile, token); equal values resolve to the smaller row
+        for (int i = et >> 5; i < own; i += 4) {
+          const int t = i * S + rank;
+          float x[4];
+          unpack4(reinterpret_cast<const uint2*>(stile)[t * 32 + lane], x);
+          unsigned long long best = 0ull;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const unsigned long long key = argmax_key(x[e], static_cast<uint32_t>(tile * 128 + lane * 4 + e));
+            best = key > best ? key : best;
+          }
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) {
+            const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, best, off);
+            best = o > best ? o : best;
+          }
+          if (lane == 0) atomicMax(p.am_keys + t, best);
+        }
+      }
     } else if (p.epi == RT_EPI_SILU_MUL) {
       for (int i = et; i < own * 8; i += 128) {
         const int t = (i >> 3) * S + rank, c = i & 7;
@@ -405,7 +448,7 @@ int max_active_clusters(int cluster, size_t smem, int tiles) {
   const auto key = std::make_pair(cluster, smem);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
-  set_smem_limit(linear_kernel<false>, smem);
+  set_smem_limit(linear_kernel<kPlain>, smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(tiles, cluster);
   cfg.blockDim = dim3(kLinThreads);
@@ -418,7 +461,7 @@ int max_active_clusters(int cluster, size_t smem, int tiles) {
   cfg.attrs = &attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, linear_kernel<false>, &cfg) != cudaSuccess) {
+  if (cudaOccupancyMaxActiveClusters(&n, linear_kernel<kPlain>, &cfg) != cudaSuccess) {
     cudaGetLastError();
     n = 0;
   }
@@ -545,9 +588,9 @@ extern "C" int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* 
   p.ld_out = ld_out;
   if (qkv) p.qkv = *qkv;
   p.status = status;
-  set_smem_limit(linear_kernel<false>, pl.smem);
+  set_smem_limit(linear_kernel<kPlain>, pl.smem);
   static const XSources no_sources{};
-  return record_cuda(launch_ex(linear_kernel<false>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
+  return record_cuda(launch_ex(linear_kernel<kPlain>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
                                static_cast<cudaStream_t>(stream), pl.splits, tw, tx, no_sources, p));
 }
 
@@ -595,7 +638,60 @@ extern "C" int rt_linear_gather(const void* const* x_ranks, int world, int cols_
   p.g_flags = flags_local;
   p.g_epoch = epoch_dev;
   p.g_epoch_add = epoch_add;
-  set_smem_limit(linear_kernel<true>, pl.smem);
-  return record_cuda(launch_ex(linear_kernel<true>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
+  set_smem_limit(linear_kernel<kGatherX>, pl.smem);
+  return record_cuda(launch_ex(linear_kernel<kGatherX>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
                                static_cast<cudaStream_t>(stream), pl.splits, tw, xs.map[0], xs, p));
+}
+
+namespace rt {
+namespace {
+__global__ void argmax_index_kernel(const unsigned long long* keys, int n, int64_t* index) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) index[i] = keys[i] == 0ull ? -1 : static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(keys[i]));
+}
+}  // namespace
+}  // namespace rt
+
+extern "C" int rt_linear_argmax(const void* x, int64_t ld_x, int m, int k, const void* w, int n_out, void* out,
+                                int64_t ld_out, void* keys, int64_t* index, int* status, rt_stream_t stream) {
+  Plan pl;
+  int rc = make_plan(m, n_out, k, RT_EPI_STORE, &pl, true);
+  if (rc != RT_OK) return rc;
+  if (!x || !w || !al16(x) || !al16(w) || ld_x < k || (ld_x * 2) % 16) return RT_ERR_INVALID_ARGUMENT;
+  if (!out || !al16(out) || ld_out < n_out || (ld_out * 2) % 16) return RT_ERR_INVALID_ARGUMENT;
+  if (!keys || (reinterpret_cast<uintptr_t>(keys) & 7) || !index) return RT_ERR_INVALID_ARGUMENT;
+  CUtensorMap tw, tx;
+  rc = make_bf16_2d_tmap(&tw, w, n_out, k, k, 128);
+  if (rc != RT_OK) return rc;
+  rc = make_bf16_2d_tmap(&tx, x, m, k, ld_x, static_cast<uint32_t>(pl.chunk_rows));
+  if (rc != RT_OK) return rc;
+  LinearParams p{};
+  p.m = m;
+  p.n_out = n_out;
+  p.k = k;
+  p.chunks = pl.chunks;
+  p.chunk_rows = pl.chunk_rows;
+  p.kblocks = pl.kblocks;
+  p.splits = pl.splits;
+  p.per = pl.per;
+  p.tiles = pl.tiles;
+  p.epi = RT_EPI_STORE;
+  p.stages = pl.stages;
+  p.stage_bytes = pl.stage_bytes;
+  p.bps = pl.bps;
+  p.tmem_cols = pl.tmem_cols;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.ld_out = ld_out;
+  p.status = status;
+  p.am_keys = static_cast<unsigned long long*>(keys);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rc = record_cuda(cudaMemsetAsync(keys, 0, static_cast<size_t>(m) * 8, s));
+  if (rc != RT_OK) return rc;
+  set_smem_limit(linear_kernel<kArgmax>, pl.smem);
+  static const XSources no_sources{};
+  rc = record_cuda(launch_ex(linear_kernel<kArgmax>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem, s,
+                             pl.splits, tw, tx, no_sources, p));
+  if (rc != RT_OK) return rc;
+  argmax_index_kernel<<<(m + 127) / 128, 128, 0, s>>>(static_cast<const unsigned long long*>(keys), m, index);
+  return check_launch();
 }

@@ -115,7 +115,7 @@ class _Layer:
 class FusedTarget:
     def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto",
                  capture_layers=None, attn_l2_prefetch: int | None = None, l2_stream: bool | None = None,
-                 l2_stream_budget: int = 64 << 20, exchange: str = "nccl"):
+                 l2_stream_budget: int = 64 << 20, exchange: str = "nccl", argmax: bool = False):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -217,6 +217,11 @@ class FusedTarget:
                           "o": [(L.gate_up_w[head // nb(L.gate_up_w[0]):], min(gu - head, cap))] if gu > head else [],
                           "gate_up": [(L.down_w, min(nb(L.down_w), cap))],
                           "down": [(nxt, min(nb(nxt), cap))]}
+        # the lm_head projection also returns each node's argmax (rt_linear_argmax):
+        # the temperature-0 posterior without a pass over the logits
+        self.argmax = bool(argmax)
+        self.posterior = torch.empty(self.n_max, dtype=torch.int64, device=dev) if self.argmax else None
+        self.last_posterior = None
         # under a KV-head split: the attention outputs' all-gather before o_proj,
         # NCCL ("nccl"), this package's peer-memory exchange ("p2p", retree_b200.peer),
         # or that exchange pulled by the o_proj kernel itself ("p2p_fused")
@@ -443,7 +448,12 @@ class FusedTarget:
         if j is not None:
             # HF's last hidden state is the final norm's output (utils/output_capturing.py:253-258)
             self.hidden_out[:n, j * hid: (j + 1) * hid].copy_(xn)
-        logits = self._linear(xn, self.lm_head, None, self.logits[:n], kind="lm_head")
+        self.last_posterior = None
+        if self.argmax and kernels.linear_supported(n, self.lm_head.shape[0], self.lm_head.shape[1], 0):
+            logits = self.logits[:n]
+            self.last_posterior = kernels.linear_argmax(xn, self.lm_head, logits, self.posterior[:n])
+        else:
+            logits = self._linear(xn, self.lm_head, None, self.logits[:n], kind="lm_head")
         if self._side is not None:
             torch.cuda.current_stream(self.device).wait_stream(self._side)  # rejoin (graph capture needs it)
         return logits

@@ -549,6 +549,28 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ep
 # ---------------------------------------------------------------------------
 # Target-gated sibling-recovery walk (rt_recovery_walk)
 # ---------------------------------------------------------------------------
+def linear_argmax(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """``out [m, n_out] = x @ w^T`` (rt_linear) and ``index [m]`` = each row's argmax (first largest; NaN
+    largest) from the same launch (rt_linear_argmax): the temperature-0 posterior without a pass over
+    the logits."""
+    _require_cuda(x, w, out, index)
+    if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or x.dim() != 2 or x.stride(-1) != 1:
+        raise RuntimeError("linear_argmax takes bf16 x [m, k] with unit inner stride")
+    if not w.is_contiguous() or out.dtype != torch.bfloat16 or out.stride(-1) != 1:
+        raise RuntimeError("linear_argmax: contiguous bf16 weights, bf16 out with unit inner stride")
+    if index.dtype != torch.int64 or not index.is_contiguous() or index.numel() < x.shape[0]:
+        raise RuntimeError("index must be contiguous int64 [m]")
+    m, k = x.shape
+    n_out = w.shape[0]
+    keys = _STATE.buffer(x.device, "argmax_keys", max(8 * m, 256))
+    _lib.check(_lib.load().rt_linear_argmax(x.data_ptr(), x.stride(0), m, k, w.data_ptr(), n_out, out.data_ptr(),
+                                            out.stride(0), keys.data_ptr(), index.data_ptr(),
+                                            status_tensor(x.device).data_ptr(), _stream(x.device)),
+               "rt_linear_argmax")
+    _count(2)  # the projection and the index conversion (the key reset is a memset)
+    return index
+
+
 def recovery_walk(parents: torch.Tensor, tokens: torch.Tensor, posterior: torch.Tensor, logits: torch.Tensor,
                   table: tuple, params: dict, count: int | None = None, count_dev: torch.Tensor | None = None,
                   stop_ids: torch.Tensor | None = None, log: tuple | None = None, out: dict | None = None,

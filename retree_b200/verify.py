@@ -59,7 +59,8 @@ class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
                  temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None,
                  gemm: str = "auto", fused_draft: bool = False, attn_l2_prefetch: int | None = None,
-                 l2_stream: bool | None = None, exchange: str = "nccl", chain: bool = False):
+                 l2_stream: bool | None = None, exchange: str = "nccl", chain: bool = False,
+                 fused_argmax: bool = False):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -124,7 +125,8 @@ class TreeVerifier:
                      and not hasattr(target, "_rt_local_kv_heads"))
         self.fused = (fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm,
                                             capture_layers=target_layer_ids, attn_l2_prefetch=attn_l2_prefetch,
-                                            l2_stream=l2_stream, exchange=exchange)
+                                            l2_stream=l2_stream, exchange=exchange,
+                                            argmax=fused_argmax and self.temperature < 1e-5)
                       if fused else None)
         # draft forward: the DFlash module (reference layout) on the fused stages
         # (retree_b200.draft.FusedDraft) when asked for and supported
@@ -213,6 +215,12 @@ class TreeVerifier:
                                     freq_threshold=0 if memory is None else memory.freq_threshold)
         self.graph = None
 
+    def _posterior(self, logits: torch.Tensor) -> torch.Tensor:
+        """Target token per node, ``[1, n]``: the fused lm_head's argmax when it ran, else sample(logits)."""
+        if self.fused is not None and self.fused.last_posterior is not None:
+            return self.fused.last_posterior.unsqueeze(0)
+        return sample(logits, self.temperature)
+
     def _walk_and_commit(self, posterior: torch.Tensor, logits: torch.Tensor, count: int) -> None:
         """Exact or recovery walk over the round's tree; commits to the output ids and start_dev."""
         if self.recovery is None:
@@ -243,7 +251,7 @@ class TreeVerifier:
             mask = attach(bits.view(1, 1, n, self.words), bits, prefix_dev=self.start_dev[:1])
             logits = self.target(ids, position_ids=pos, attention_mask=mask, past_key_values=self.cache,
                                  use_cache=True).logits
-        posterior = sample(logits, self.temperature)
+        posterior = self._posterior(logits)
         self._walk_and_commit(posterior[0], logits[0], count)
         kernels.kv_compact(self.cache.slab, 0, self.walk["accepted"], cur_length=n,
                            n_keep_dev=self.walk["accepted_len"], n_keep=n, past_len_dev=self.start_dev[1:2])
@@ -321,7 +329,7 @@ class TreeVerifier:
                               use_cache=True, output_hidden_states=self.target_layer_ids is not None)
         t = self._tick("verify", t)
         # 3.-5. posterior, walk, commit, compaction
-        posterior = sample(out.logits, self.temperature)
+        posterior = self._posterior(out.logits)
         if self.debug:
             self.last_posterior = posterior
             self.last_slab = self.cache.slab[:, :, : start + n, :].clone()
