@@ -37,6 +37,7 @@
 #include <map>
 #include <mutex>
 
+#include "argmax_key.cuh"
 #include "common.cuh"
 #include "host_util.h"
 #include "layer_math.cuh"
@@ -110,21 +111,6 @@ constexpr uint32_t kPartBytes = 32 * 128 * 4;  // one 32-token fp32 partial slic
 // kMode: kPlain, kGatherX (X gathered from the ranks of a split, rt_linear_gather)
 // or kArgmax (store + per-token argmax keys, rt_linear_argmax).
 constexpr int kPlain = 0, kGatherX = 1, kArgmax = 2;
-
-// Order-preserving key of a logit for the argmax: larger value -> larger key,
-// -0.0 == +0.0, NaN above every number (torch.argmax returns a NaN's index);
-// the low half favours the smaller row on equal values.
-__device__ __forceinline__ unsigned long long argmax_key(float x, uint32_t row) {
-  uint32_t b = __float_as_uint(x);
-  uint32_t k;
-  if (x != x) {
-    k = 0xFFFFFFFFu;
-  } else {
-    if (b == 0x80000000u) b = 0u;
-    k = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
-  }
-  return (static_cast<unsigned long long>(k) << 32) | (0xFFFFFFFFu - row);
-}
 
 template <int kMode>
 __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
@@ -647,7 +633,7 @@ namespace rt {
 namespace {
 __global__ void argmax_index_kernel(const unsigned long long* keys, int n, int64_t* index) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) index[i] = keys[i] == 0ull ? -1 : static_cast<int64_t>(0xFFFFFFFFu - static_cast<uint32_t>(keys[i]));
+  if (i < n) index[i] = argmax_row(keys[i]);
 }
 }  // namespace
 }  // namespace rt
