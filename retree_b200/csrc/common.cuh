@@ -121,6 +121,22 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
+// Wait (bounded, ignoring the abort flag) for copies a CTA issued itself to
+// land before it exits, so no TMA write reaches shared memory after the block
+// is gone.  Used only on the abort path, where mbar_wait would return early.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
+}
+
+// Count `bytes` of a phase's expected transaction bytes as arrived without a
+// copy: a producer that gave up before issuing some loads of an armed stage
+// lets the stage's barrier complete (its contents are then not to be used).
+__device__ __forceinline__ void mbar_complete_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.complete_tx.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }

@@ -178,7 +178,11 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
           if constexpr (kGather) {
             const int src = (kx / kBK) / p.g_blocks;
             if (!(ready & (1u << src))) {
-              if (!wait_peer_flag(p.g_flags + src, epoch, abort_flag, p.status)) return false;
+              if (!wait_peer_flag(p.g_flags + src, epoch, abort_flag, p.status)) {
+                // the stage was armed for these X bytes: count them so its barrier completes
+                mbar_complete_tx(&bar.full[s], static_cast<uint32_t>((p.bps - b) * p.chunks * p.chunk_rows * 128));
+                return false;
+              }
               ready |= 1u << src;
             }
             const int lx = kx - src * p.g_blocks * kBK;
@@ -200,8 +204,17 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
       pdl_wait();
       if constexpr (kGather) epoch = *p.g_epoch + p.g_epoch_add;
       int issued = pre;
-      for (int it = 0; it < pre; ++it)
+      int xs = 0;  // first-pass stages whose X loads went out
+      for (int it = 0; it < pre; ++it) {
         if (!load_x(it)) break;
+        xs = it + 1;
+      }
+      if constexpr (kGather) {
+        // gave up inside stage xs (load_x settled its bytes): the first-pass stages
+        // after it were armed for X that never comes
+        for (int it = xs + 1; it < pre; ++it)
+          mbar_complete_tx(&bar.full[it % p.stages], static_cast<uint32_t>(p.bps * p.chunks * p.chunk_rows * 128));
+      }
       for (int it = pre; it < nk && !(kGather && *abort_flag); ++it) {
         const int s = it % p.stages;
         if (!mbar_wait(&bar.empty[s], ((it / p.stages) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
@@ -212,7 +225,7 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
       if (*abort_flag) {
         // let the copies still in flight land before the block's memory goes away
         for (int it = max(0, issued - p.stages); it < issued; ++it)
-          mbar_wait(&bar.full[it % p.stages], (it / p.stages) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+          mbar_wait_drain(&bar.full[it % p.stages], (it / p.stages) & 1);
       }
     } else {
       pdl_wait();
@@ -242,6 +255,9 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
       }
       // arrives once every MMA issued above has completed (also on the abort path)
       umma_commit(&bar.acc);
+      // the TMEM is freed after the final block barrier: on the abort path the
+      // epilogue does not wait for the accumulator, so this lane does
+      if (*abort_flag) mbar_wait_drain(&bar.acc, 0);
     }
   } else {
     pdl_wait();

@@ -273,9 +273,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       if (!q_issued) issue_q();
       if (*abort_flag) {
-        mbar_wait(&bar.full_q, 0, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
-        for (int j = max(0, issued - 2); j < issued; ++j)
-          mbar_wait(&bar.full_k[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+        mbar_wait_drain(&bar.full_q, 0);
+        for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_drain(&bar.full_k[j & 1], (j >> 1) & 1);
       }
     } else if (lane == 1) {
       int issued = 0;
@@ -297,8 +296,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         issued = j + 1;
       }
       if (*abort_flag)
-        for (int j = max(0, issued - 2); j < issued; ++j)
-          mbar_wait(&bar.full_v[j & 1], (j >> 1) & 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+        for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_drain(&bar.full_v[j & 1], (j >> 1) & 1);
       pdl_wait();
     } else {
       pdl_wait();
@@ -357,7 +355,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       // all issued MMAs complete before TMEM is released
       umma_commit(&bar.fin);
-      mbar_wait(&bar.fin, 0, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
+      mbar_wait_drain(&bar.fin, 0);  // also on the abort path: no MMA may outlive the TMEM
     }
   } else {
     // ---------------- softmax / epilogue (warps 0-7) ----------------
