@@ -83,6 +83,8 @@ def parse():
                     help="MB of the following projections' weights each attention launch warms in L2")
     ap.add_argument("--l2-stream", action="store_true",
                     help="warm the next projection's weights in L2 from a side stream next to each launch")
+    ap.add_argument("--kv-l2-prefetch", action="store_true",
+                    help="the QKV projection (rt_linear) warms the L2 with the layer's K/V prefix for the attention")
     ap.add_argument("--fused-argmax", action="store_true",
                     help="the lm_head projection also returns the posterior (rt_linear_argmax), no argmax pass")
     ap.add_argument("--recovery", action="store_true",
@@ -297,7 +299,8 @@ def run_ours(args, wl, rank, world, local_rank):
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
                          fused=not args.hf_forward, gemm=args.gemm,
                          attn_l2_prefetch=int(args.attn_l2_prefetch * 2**20), l2_stream=args.l2_stream,
-                         exchange=args.exchange, fused_argmax=args.fused_argmax)
+                         exchange=args.exchange, fused_argmax=args.fused_argmax,
+                         kv_l2_prefetch=args.kv_l2_prefetch)
         if wl.get("split"):
             v.prefill_random(plen, seed=req)
         else:
@@ -504,6 +507,7 @@ def run_ours(args, wl, rank, world, local_rank):
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
                    "projections": projections,
                    "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
+                   "kv_prefix_l2_warm_up": args.kv_l2_prefetch,
                    "walk": "target-gated sibling recovery (device)" if args.recovery else "exact",
                    "posterior": "argmax fused into the lm_head projection" if args.fused_argmax else "torch.argmax",
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "

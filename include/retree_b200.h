@@ -411,7 +411,12 @@ int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, rt_stream_t
  *                    (Qwen3MLP.forward, modeling_qwen3.py:81-83);
  *   RT_EPI_QKV_ROPE  W = [Wq; Wk; Wv] (n_out = (Hq + 2 Hkv) * 128): what
  *                    rt_qk_norm_rope_append does with the bf16 result, with
- *                    the arguments of *qkv (out / ld_out unused).
+ *                    the arguments of *qkv (out / ld_out unused);
+ *   RT_EPI_QKV_ROPE_KV_WARM  the same, and while the weights stream the
+ *                    launch asks the L2 for the K/V rows [0, prefix) of every
+ *                    kv head of *qkv's cache (prefix = offset + *offset_dev),
+ *                    which the attention reads next (cp.async.bulk.prefetch.L2,
+ *                    nothing waits; Hkv <= 8).
  * When 128-row tiles alone do not cover the GPU, K is split over a cluster
  * of up to 8 CTAs whose partial sums are added in a fixed order over
  * distributed shared memory: no workspace, results independent of timing.
@@ -420,6 +425,7 @@ int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, rt_stream_t
 #define RT_EPI_STORE 0
 #define RT_EPI_SILU_MUL 1
 #define RT_EPI_QKV_ROPE 2
+#define RT_EPI_QKV_ROPE_KV_WARM 3
 
 typedef struct rt_qkv_epilogue {
   int num_q_heads;

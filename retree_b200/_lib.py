@@ -69,6 +69,7 @@ SIGNATURES = {
 RT_EPI_STORE = 0
 RT_EPI_SILU_MUL = 1
 RT_EPI_QKV_ROPE = 2
+RT_EPI_QKV_ROPE_KV_WARM = 3
 
 
 RT_L2_MAX_RANGES = 16

@@ -42,21 +42,25 @@ inline int l2_ranges_from(const rt_l2_ranges* in, L2Ranges* out) {
   return RT_OK;
 }
 
-// Requests for CTA `cta` of `ctas`'s share of every range -- bytes
-// [cta*per, (cta+1)*per) -- in 32 KB pieces spread over `parts` threads.
-__device__ __forceinline__ void l2_warm_share(const L2Ranges& r, int64_t cta, int64_t ctas, int part, int parts) {
+// Requests for CTA `cta` of `ctas`'s share of one range (16-byte aligned,
+// `bytes` a multiple of 16) -- bytes [cta*per, (cta+1)*per) -- in 32 KB
+// pieces spread over `parts` threads.
+__device__ __forceinline__ void l2_warm_range(const char* ptr, int64_t bytes, int64_t cta, int64_t ctas, int part,
+                                              int parts) {
   constexpr int64_t kPiece = 32768;
-  for (int i = 0; i < r.count; ++i) {
-    const int64_t bytes = r.bytes[i];
-    if (r.ptr[i] == nullptr || bytes <= 0) continue;
-    const int64_t per = (((bytes + ctas - 1) / ctas) + 15) & ~static_cast<int64_t>(15);
-    const int64_t b0 = cta * per, b1 = bytes < b0 + per ? bytes : b0 + per;
-    for (int64_t o = b0 + static_cast<int64_t>(part) * kPiece; o < b1; o += static_cast<int64_t>(parts) * kPiece) {
-      const int64_t len = kPiece < b1 - o ? kPiece : b1 - o;
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(r.ptr[i] + o), "r"(static_cast<uint32_t>(len))
-                   : "memory");
-    }
+  if (ptr == nullptr || bytes <= 0) return;
+  const int64_t per = (((bytes + ctas - 1) / ctas) + 15) & ~static_cast<int64_t>(15);
+  const int64_t b0 = cta * per, b1 = bytes < b0 + per ? bytes : b0 + per;
+  for (int64_t o = b0 + static_cast<int64_t>(part) * kPiece; o < b1; o += static_cast<int64_t>(parts) * kPiece) {
+    const int64_t len = kPiece < b1 - o ? kPiece : b1 - o;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr + o), "r"(static_cast<uint32_t>(len))
+                 : "memory");
   }
+}
+
+// The same for every range of `r`.
+__device__ __forceinline__ void l2_warm_share(const L2Ranges& r, int64_t cta, int64_t ctas, int part, int parts) {
+  for (int i = 0; i < r.count; ++i) l2_warm_range(r.ptr[i], r.bytes[i], cta, ctas, part, parts);
 }
 
 // ---------------------------------------------------------------------------

@@ -228,6 +228,21 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
           mbar_wait_drain(&bar.full[it % p.stages], (it / p.stages) & 1);
       }
     } else {
+      if (p.epi == RT_EPI_QKV_ROPE_KV_WARM) {
+        // the attention that follows reads this layer's K/V prefix: ask the L2 for this
+        // CTA's share of it now (the prefix rows are not written during the forward, so
+        // before the dependency wait); ranges K head 0..Hkv-1, then V
+        const rt_qkv_epilogue& e = p.qkv;
+        const int64_t prefix = e.offset + (e.offset_dev != nullptr ? *e.offset_dev : 0);
+        const int64_t bytes = (prefix > 0 && prefix <= e.capacity ? prefix : 0) * e.cache_row_stride;
+        const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) * blockIdx.y;
+        const int64_t ctas = static_cast<int64_t>(gridDim.x) * gridDim.y;
+        for (int r = 0; r < 2 * e.num_kv_heads; ++r) {
+          const char* base = static_cast<const char*>(r < e.num_kv_heads ? e.k_cache : e.v_cache) +
+                             (r % e.num_kv_heads) * e.cache_head_stride;
+          l2_warm_range(base, bytes, cta, ctas, lane - 1, 31);
+        }
+      }
       pdl_wait();
     }
   } else if (warp == 1) {
@@ -477,7 +492,7 @@ int max_active_clusters(int cluster, size_t smem, int tiles) {
 // with the deeper one-CTA-per-SM ring preferred over two CTAs per SM.
 int make_plan(int m, int n_out, int k, int epi, Plan* pl, bool choose) {
   if (m <= 0 || m > kMaxTokens || k < 8 || k % 8 || n_out <= 0 || n_out % 128) return RT_ERR_INVALID_ARGUMENT;
-  if (epi < RT_EPI_STORE || epi > RT_EPI_QKV_ROPE) return RT_ERR_INVALID_ARGUMENT;
+  if (epi < RT_EPI_STORE || epi > RT_EPI_QKV_ROPE_KV_WARM) return RT_ERR_INVALID_ARGUMENT;
   const int m_pad = (m + 15) / 16 * 16;
   pl->chunks = m_pad > 256 ? 2 : 1;
   pl->chunk_rows = pl->chunks == 1 ? m_pad : ((m_pad / 2 + 15) / 16 * 16);
@@ -553,12 +568,15 @@ extern "C" int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* 
   int rc = make_plan(m, n_out, k, epilogue, &pl, true);
   if (rc != RT_OK) return rc;
   if (!x || !w || !al16(x) || !al16(w) || ld_x < k || (ld_x * 2) % 16) return RT_ERR_INVALID_ARGUMENT;
-  if (epilogue == RT_EPI_QKV_ROPE) {
+  if (epilogue == RT_EPI_QKV_ROPE || epilogue == RT_EPI_QKV_ROPE_KV_WARM) {
     if (!qkv || qkv->num_q_heads <= 0 || qkv->num_kv_heads <= 0 ||
         n_out != (qkv->num_q_heads + 2 * qkv->num_kv_heads) * 128 || !qkv->cos_table || !qkv->sin_table ||
         qkv->table_len <= 0 || !qkv->positions || !qkv->q_out || !qkv->k_cache || !qkv->v_cache ||
         qkv->capacity <= 0 || (qkv->q_norm_weight == nullptr) != (qkv->k_norm_weight == nullptr) ||
         qkv->cache_head_stride % 8 || qkv->cache_row_stride % 8 ||
+        (epilogue == RT_EPI_QKV_ROPE_KV_WARM &&
+         (qkv->num_kv_heads > 8 || qkv->cache_row_stride % 16 || qkv->cache_head_stride % 16 ||
+          reinterpret_cast<uintptr_t>(qkv->k_cache) % 16 || reinterpret_cast<uintptr_t>(qkv->v_cache) % 16)) ||
         reinterpret_cast<uintptr_t>(qkv->k_cache) % 8 || reinterpret_cast<uintptr_t>(qkv->v_cache) % 8 ||
         reinterpret_cast<uintptr_t>(qkv->q_out) % 8)
       return RT_ERR_INVALID_ARGUMENT;

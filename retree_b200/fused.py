@@ -115,7 +115,8 @@ class _Layer:
 class FusedTarget:
     def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto",
                  capture_layers=None, attn_l2_prefetch: int | None = None, l2_stream: bool | None = None,
-                 l2_stream_budget: int = 64 << 20, exchange: str = "nccl", argmax: bool = False):
+                 l2_stream_budget: int = 64 << 20, exchange: str = "nccl", argmax: bool = False,
+                 kv_l2_prefetch: bool | None = None):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -217,6 +218,11 @@ class FusedTarget:
                           "o": [(L.gate_up_w[head // nb(L.gate_up_w[0]):], min(gu - head, cap))] if gu > head else [],
                           "gate_up": [(L.down_w, min(nb(L.down_w), cap))],
                           "down": [(nxt, min(nb(nxt), cap))]}
+        # the QKV projection (on rt_linear) asks the L2 for the layer's K/V prefix while
+        # its weights stream (RT_EPI_QKV_ROPE_KV_WARM), so the attention reads it from L2
+        if kv_l2_prefetch is None:
+            kv_l2_prefetch = os.environ.get("RETREE_B200_KV_L2PF", "0") not in ("", "0")
+        self.kv_l2_prefetch = bool(kv_l2_prefetch)
         # the lm_head projection also returns each node's argmax (rt_linear_argmax):
         # the temperature-0 posterior without a pass over the logits
         self.argmax = bool(argmax)
@@ -353,7 +359,8 @@ class FusedTarget:
         n = xn.shape[0]
         kc, vc = self.cache.slab[2 * L.index], self.cache.slab[2 * L.index + 1]
         if self.use_rt["qkv"] and L.qkv_b is None and kernels.linear_supported(n, L.qkv_w.shape[0], xn.shape[1], 2):
-            kernels.linear(xn, L.qkv_w, epilogue=2,
+            # epilogue 3 also warms the L2 with this layer's K/V prefix for the attention that follows
+            kernels.linear(xn, L.qkv_w, epilogue=3 if self.kv_l2_prefetch and L.hkv <= 8 else 2,
                            qkv=dict(num_q_heads=L.hq, num_kv_heads=L.hkv, q_norm=L.q_norm, k_norm=L.k_norm,
                                     eps=L.eps_qk, cos=self.cos, sin=self.sin, positions=positions, q_out=self.q[:n],
                                     k_cache=kc, v_cache=vc, offset=offset, offset_dev=offset_dev))

@@ -503,7 +503,8 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ep
     silu(gate) * up``; 2 (w = [Wq; Wk; Wv]): head norms + rotary, q to
     ``qkv['q_out']``, k/v into the cache (keys of ``qkv`` as in
     ``qk_norm_rope_append``: num_q_heads, num_kv_heads, q_norm, k_norm, eps,
-    cos, sin, positions, q_out, k_cache, v_cache, offset, offset_dev).
+    cos, sin, positions, q_out, k_cache, v_cache, offset, offset_dev); 3: as 2,
+    and the launch warms the L2 with the cache's K/V prefix rows.
     """
     lib = _lib.load()
     _require_cuda(x, w, out)
@@ -520,7 +521,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ep
         raise RuntimeError(f"rt_linear does not take m={m}, n_out={n_out}, k={k}")
     epi = None
     keep = []
-    if epilogue == _lib.RT_EPI_QKV_ROPE:
+    if epilogue in (_lib.RT_EPI_QKV_ROPE, _lib.RT_EPI_QKV_ROPE_KV_WARM):
         kc, vc = qkv["k_cache"], qkv["v_cache"]
         es = kc.element_size()
         epi = _lib.QkvEpilogue(qkv["num_q_heads"], qkv["num_kv_heads"], _ptr(qkv.get("q_norm")),

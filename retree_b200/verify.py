@@ -60,7 +60,7 @@ class TreeVerifier:
                  temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None,
                  gemm: str = "auto", fused_draft: bool = False, attn_l2_prefetch: int | None = None,
                  l2_stream: bool | None = None, exchange: str = "nccl", chain: bool = False,
-                 fused_argmax: bool = False):
+                 fused_argmax: bool = False, kv_l2_prefetch: bool | None = None):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -126,7 +126,8 @@ class TreeVerifier:
         self.fused = (fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm,
                                             capture_layers=target_layer_ids, attn_l2_prefetch=attn_l2_prefetch,
                                             l2_stream=l2_stream, exchange=exchange,
-                                            argmax=fused_argmax and self.temperature < 1e-5)
+                                            argmax=fused_argmax and self.temperature < 1e-5,
+                                            kv_l2_prefetch=kv_l2_prefetch)
                       if fused else None)
         # draft forward: the DFlash module (reference layout) on the fused stages
         # (retree_b200.draft.FusedDraft) when asked for and supported

@@ -94,6 +94,8 @@ def test_linear_shape_checks_without_gpu():
                          (256, 128), (384, 256), (1536, 512)):
             for epi in (0, 1):
                 assert lib.rt_linear_check(m, n_out, k, epi) == 0, (m, n_out, k, epi)
+    assert lib.rt_linear_check(17, 6144, 2560, 3) == 0  # QKV epilogue with the K/V prefix warm-up
+    assert lib.rt_linear_check(17, 6144, 2560, 4) != 0
     assert lib.rt_linear_check(513, 128, 64, 0) != 0
     assert lib.rt_linear_check(17, 200, 64, 0) != 0
     assert lib.rt_linear_check(17, 256, 60, 0) != 0

@@ -86,3 +86,31 @@ def test_side_stream_warm_up_changes_no_round(monkeypatch):
     s = plain.start
     assert torch.equal(plain.output_ids[: s + 1], warm.output_ids[: s + 1])
     assert torch.equal(plain.cache.slab[:, :, :s], warm.cache.slab[:, :, :s])
+
+
+@torch.inference_mode()
+def test_kv_prefix_warm_up_in_the_qkv_projection_changes_nothing():
+    """RT_EPI_QKV_ROPE_KV_WARM (the QKV projection also asks the L2 for the K/V prefix) writes what
+    RT_EPI_QKV_ROPE writes, and a fused forward with it gives the same logits."""
+    dev = cuda()
+    cfg = qwen3_config("small", hidden_size=512, intermediate_size=1024, num_hidden_layers=2, num_attention_heads=8,
+                       num_key_value_heads=2, vocab_size=2000, tie_word_embeddings=False)
+    model = build_target(cfg, device=dev, seed=3)
+    L, n = 300, 17
+    outs = []
+    for warm in (False, True):
+        cache = TreeKVCache.for_model(model.config, capacity=512, device=dev)
+        cache.slab.copy_(torch.randn(cache.slab.shape, device=dev,
+                                     generator=torch.Generator(device=dev).manual_seed(1)).to(torch.bfloat16))
+        ft = fused.FusedTarget(model, cache, n_max=32, gemm="tcgen05", kv_l2_prefetch=warm)
+        tok = torch.randint(0, 2000, (n,), device=dev, generator=torch.Generator(device=dev).manual_seed(3))
+        pos = torch.arange(L, L + n, device=dev)
+        bits = bits_tensor(random_tree(4, n - 1)[1], dev)
+        for offset_dev in (None, torch.tensor([L], dtype=torch.int64, device=dev)):
+            if offset_dev is None:
+                outs.append(ft.forward(tok, pos, bits, offset=L).clone())
+            else:
+                outs.append(ft.forward(tok, pos, bits, offset_dev=offset_dev).clone())
+        outs.append(cache.slab[:, :, : L + n].clone())
+    kernels.check_device_status(dev)
+    assert all(torch.equal(a, b) for a, b in zip(outs[:3], outs[3:]))
