@@ -83,6 +83,8 @@ def parse():
                     help="MB of the following projections' weights each attention launch warms in L2")
     ap.add_argument("--l2-stream", action="store_true",
                     help="warm the next projection's weights in L2 from a side stream next to each launch")
+    ap.add_argument("--linear-warm", action="store_true",
+                    help="rt_linear launches ask the L2 for each CTA's weight rows at entry (long DRAM runs)")
     ap.add_argument("--kv-l2-prefetch", action="store_true",
                     help="the QKV projection (rt_linear) warms the L2 with the layer's K/V prefix for the attention")
     ap.add_argument("--fused-argmax", action="store_true",
@@ -271,6 +273,8 @@ def run_ours(args, wl, rank, world, local_rank):
     from retree_b200.verify import TreeVerifier
 
     os.environ["DDTREE_TREE_STRATEGY"] = args.strategy
+    if args.linear_warm:
+        kernels.set_linear_weight_warm(True)
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     cfg = qwen3_config(wl["model"])
@@ -507,7 +511,7 @@ def run_ours(args, wl, rank, world, local_rank):
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
                    "projections": projections,
                    "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
-                   "kv_prefix_l2_warm_up": args.kv_l2_prefetch,
+                   "kv_prefix_l2_warm_up": args.kv_l2_prefetch, "linear_weight_warm_up": args.linear_warm,
                    "walk": "target-gated sibling recovery (device)" if args.recovery else "exact",
                    "posterior": "argmax fused into the lm_head projection" if args.fused_argmax else "torch.argmax",
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "

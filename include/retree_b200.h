@@ -62,6 +62,15 @@ const char* rt_status_string(int code);
 void rt_set_pdl(int enabled);
 int rt_pdl_enabled(void);
 
+/* rt_linear launches (all modes) with the weight-row L2 warm-up: at entry the
+ * producer warp's idle lanes ask the L2 (cp.async.bulk.prefetch.L2) for each
+ * of the CTA's 128 weight rows over its whole K range, one contiguous request
+ * per row, so the ring's 128-byte-wide TMA boxes hit L2 and the DRAM sees long
+ * runs.  Off by default (RETREE_B200_LINEAR_WARM=1 turns it on); no result
+ * depends on it.  No counterpart in the reference. */
+void rt_set_linear_weight_warm(int enabled);
+int rt_linear_weight_warm_enabled(void);
+
 /* ------------------------------------------------------------------------
  * KV-cache compaction after a commit.
  * Replaces compact_tail_inplace / _compact_appended_window

@@ -27,6 +27,8 @@ SIGNATURES = {
     "rt_status_string": (ctypes.c_char_p, [_I]),
     "rt_set_pdl": (None, [_I]),
     "rt_pdl_enabled": (_I, []),
+    "rt_set_linear_weight_warm": (None, [_I]),
+    "rt_linear_weight_warm_enabled": (_I, []),
     "rt_kv_compact": (_I, [_P, _P, _I, _I64, _I, _I64, _I64, _I, _I64, _P, _I64, _P, _I, _P, _P, _P]),
     "rt_kv_append": (_I, [_P, _P, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P]),
     "rt_tree_attn_workspace_size": (_SZ, [_I, _I, _I, _I, _I64, _I]),

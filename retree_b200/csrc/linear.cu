@@ -70,6 +70,9 @@ struct LinearParams {
   int64_t g_epoch_add;
   // rt_linear_argmax: per token the max of argmax_key over the output row (zeroed before the launch)
   unsigned long long* am_keys;
+  // weight-row L2 warm-up at entry (rt_set_linear_weight_warm)
+  int w_warm;
+  const char* w_ptr;
 };
 
 // X sources of rt_linear_gather: one tensor map per rank's column block
@@ -228,6 +231,15 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
           mbar_wait_drain(&bar.full[it % p.stages], (it / p.stages) & 1);
       }
     } else {
+      if (p.w_warm) {
+        // this CTA's 128 weight rows over its K range, one contiguous request per row
+        const int64_t c0 = static_cast<int64_t>(kb0) * p.bps * kBK;
+        const int64_t c1 = min(static_cast<int64_t>(kb0 + nk) * p.bps * kBK, static_cast<int64_t>(p.k));
+        for (int r = lane - 1; r < 128 && c1 > c0; r += 31) {
+          const int64_t row = dual ? (r < 64 ? tile * 64 + r : p.n_out / 2 + tile * 64 + (r - 64)) : tile * 128 + r;
+          l2_warm_range(p.w_ptr + (row * p.k + c0) * 2, (c1 - c0) * 2, 0, 1, 0, 1);
+        }
+      }
       if (p.epi == RT_EPI_QKV_ROPE_KV_WARM) {
         // the attention that follows reads this layer's K/V prefix: ask the L2 for this
         // CTA's share of it now (the prefix rows are not written during the forward, so
@@ -608,6 +620,8 @@ extern "C" int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* 
   p.ld_out = ld_out;
   if (qkv) p.qkv = *qkv;
   p.status = status;
+  p.w_warm = linear_weight_warm() ? 1 : 0;
+  p.w_ptr = static_cast<const char*>(w);
   set_smem_limit(linear_kernel<kPlain>, pl.smem);
   static const XSources no_sources{};
   return record_cuda(launch_ex(linear_kernel<kPlain>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
@@ -658,6 +672,8 @@ extern "C" int rt_linear_gather(const void* const* x_ranks, int world, int cols_
   p.g_flags = flags_local;
   p.g_epoch = epoch_dev;
   p.g_epoch_add = epoch_add;
+  p.w_warm = linear_weight_warm() ? 1 : 0;
+  p.w_ptr = static_cast<const char*>(w);
   set_smem_limit(linear_kernel<kGatherX>, pl.smem);
   return record_cuda(launch_ex(linear_kernel<kGatherX>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
                                static_cast<cudaStream_t>(stream), pl.splits, tw, xs.map[0], xs, p));
@@ -704,6 +720,8 @@ extern "C" int rt_linear_argmax(const void* x, int64_t ld_x, int m, int k, const
   p.ld_out = ld_out;
   p.status = status;
   p.am_keys = static_cast<unsigned long long*>(keys);
+  p.w_warm = linear_weight_warm() ? 1 : 0;
+  p.w_ptr = static_cast<const char*>(w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = record_cuda(cudaMemsetAsync(keys, 0, static_cast<size_t>(m) * 8, s));
   if (rc != RT_OK) return rc;

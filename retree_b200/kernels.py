@@ -82,6 +82,15 @@ def pdl_enabled() -> bool:
     return bool(_lib.load().rt_pdl_enabled())
 
 
+def set_linear_weight_warm(enabled: bool) -> None:
+    """rt_linear launches ask the L2 for each CTA's weight rows at entry (rt_set_linear_weight_warm)."""
+    _lib.load().rt_set_linear_weight_warm(int(bool(enabled)))
+
+
+def linear_weight_warm_enabled() -> bool:
+    return bool(_lib.load().rt_linear_weight_warm_enabled())
+
+
 def status_tensor(device) -> torch.Tensor:
     """The device status word the kernels of this process report into."""
     return _STATE.status(device)

@@ -205,3 +205,10 @@ int main(void) {
     want_ws = _lib.load().rt_tree_attn_workspace_size(17, 32, 8, 128, 2048, 17)
     assert out[0] == "2" and " ".join(out[1:-2]) == "invalid argument"
     assert int(out[-2]) == want_ws > 0 and out[-1] == "0"
+
+
+def test_launch_switches_without_gpu():
+    kernels.set_linear_weight_warm(True)
+    assert kernels.linear_weight_warm_enabled()
+    kernels.set_linear_weight_warm(False)
+    assert not kernels.linear_weight_warm_enabled()

@@ -114,3 +114,28 @@ def test_kv_prefix_warm_up_in_the_qkv_projection_changes_nothing():
         outs.append(cache.slab[:, :, : L + n].clone())
     kernels.check_device_status(dev)
     assert all(torch.equal(a, b) for a, b in zip(outs[:3], outs[3:]))
+
+
+@torch.inference_mode()
+def test_weight_row_warm_up_changes_no_projection():
+    """rt_set_linear_weight_warm: every rt_linear mode gives the same bits with the warm-up on."""
+    dev = cuda()
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn((17, 2560), device=dev, generator=g).to(torch.bfloat16)
+    outs = []
+    for warm in (False, True):
+        kernels.set_linear_weight_warm(warm)
+        try:
+            for n_out, k, epi in ((2560, 2560, 0), (19456, 2560, 1), (2560, 9728, 0)):
+                w = (torch.randn((n_out, k), device=dev, generator=torch.Generator(device=dev).manual_seed(n_out + k))
+                     * k ** -0.5).to(torch.bfloat16)
+                xx = x if k == 2560 else torch.randn((17, k), device=dev,
+                                                     generator=torch.Generator(device=dev).manual_seed(1)).to(
+                    torch.bfloat16)
+                outs.append(kernels.linear(xx, w, epilogue=epi).clone())
+            torch.cuda.synchronize()
+        finally:
+            kernels.set_linear_weight_warm(False)
+    kernels.check_device_status(dev)
+    half = len(outs) // 2
+    assert all(torch.equal(a, b) for a, b in zip(outs[:half], outs[half:]))
