@@ -75,11 +75,18 @@ struct LinearParams {
   const char* w_ptr;
 };
 
+// kMode: kPlain, kGatherX (X gathered from the ranks of a split, rt_linear_gather)
+// or kArgmax (store + per-token argmax keys, rt_linear_argmax).
+constexpr int kPlain = 0, kGatherX = 1, kArgmax = 2;
+
 // X sources of rt_linear_gather: one tensor map per rank's column block
-// (peer memory for the other ranks; plain, non-multicast TMA loads).
+// (peer memory for the other ranks; plain, non-multicast TMA loads).  The
+// other modes carry one unused map, not eight (1 KB less of kernel
+// parameters per launch).
 constexpr int kMaxGather = 8;
+template <int kMode>
 struct XSources {
-  CUtensorMap map[kMaxGather];
+  CUtensorMap map[kMode == kGatherX ? kMaxGather : 1];
 };
 
 constexpr uint32_t kPeerWaitLimit = 1u << 22;  // polls x ~64 ns
@@ -111,14 +118,10 @@ struct LinBars {
 
 constexpr uint32_t kPartBytes = 32 * 128 * 4;  // one 32-token fp32 partial slice (split-K exchange)
 
-// kMode: kPlain, kGatherX (X gathered from the ranks of a split, rt_linear_gather)
-// or kArgmax (store + per-token argmax keys, rt_linear_argmax).
-constexpr int kPlain = 0, kGatherX = 1, kArgmax = 2;
-
 template <int kMode>
 __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_constant__ CUtensorMap tmap_w,
                                                              const __grid_constant__ CUtensorMap tmap_x,
-                                                             const __grid_constant__ XSources xs,
+                                                             const __grid_constant__ XSources<kMode> xs,
                                                              const LinearParams p) {
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -207,15 +210,15 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
       pdl_wait();
       if constexpr (kGather) epoch = *p.g_epoch + p.g_epoch_add;
       int issued = pre;
-      int xs = 0;  // first-pass stages whose X loads went out
+      int x_stages = 0;  // first-pass stages whose X loads went out
       for (int it = 0; it < pre; ++it) {
         if (!load_x(it)) break;
-        xs = it + 1;
+        x_stages = it + 1;
       }
       if constexpr (kGather) {
-        // gave up inside stage xs (load_x settled its bytes): the first-pass stages
-        // after it were armed for X that never comes
-        for (int it = xs + 1; it < pre; ++it)
+        // gave up inside stage x_stages (load_x settled its bytes): the first-pass
+        // stages after it were armed for X that never comes
+        for (int it = x_stages + 1; it < pre; ++it)
           mbar_complete_tx(&bar.full[it % p.stages], static_cast<uint32_t>(p.bps * p.chunks * p.chunk_rows * 128));
       }
       for (int it = pre; it < nk && !(kGather && *abort_flag); ++it) {
@@ -623,7 +626,7 @@ extern "C" int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* 
   p.w_warm = linear_weight_warm() ? 1 : 0;
   p.w_ptr = static_cast<const char*>(w);
   set_smem_limit(linear_kernel<kPlain>, pl.smem);
-  static const XSources no_sources{};
+  static const XSources<kPlain> no_sources{};
   return record_cuda(launch_ex(linear_kernel<kPlain>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
                                static_cast<cudaStream_t>(stream), pl.splits, tw, tx, no_sources, p));
 }
@@ -645,7 +648,7 @@ extern "C" int rt_linear_gather(const void* const* x_ranks, int world, int cols_
   CUtensorMap tw;
   rc = make_bf16_2d_tmap(&tw, w, n_out, k, k, 128);
   if (rc != RT_OK) return rc;
-  XSources xs{};
+  XSources<kGatherX> xs{};
   for (int r = 0; r < world; ++r) {
     rc = make_bf16_2d_tmap(&xs.map[r], x_ranks[r], m, cols_per_rank, ld_x, static_cast<uint32_t>(pl.chunk_rows));
     if (rc != RT_OK) return rc;
@@ -726,7 +729,7 @@ extern "C" int rt_linear_argmax(const void* x, int64_t ld_x, int m, int k, const
   rc = record_cuda(cudaMemsetAsync(keys, 0, static_cast<size_t>(m) * 8, s));
   if (rc != RT_OK) return rc;
   set_smem_limit(linear_kernel<kArgmax>, pl.smem);
-  static const XSources no_sources{};
+  static const XSources<kArgmax> no_sources{};
   rc = record_cuda(launch_ex(linear_kernel<kArgmax>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem, s,
                              pl.splits, tw, tx, no_sources, p));
   if (rc != RT_OK) return rc;
