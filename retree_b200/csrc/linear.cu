@@ -89,7 +89,7 @@ struct XSources {
   CUtensorMap map[kMode == kGatherX ? kMaxGather : 1];
 };
 
-constexpr uint32_t kPeerWaitLimit = 1u << 22;  // polls x ~64 ns
+constexpr uint32_t kPeerWaitLimit = 1u << 22;  // polls (system-scope load + ~64 ns sleep): 0.5 s or more
 
 // Bounded wait for a peer's announcement; on success the async proxy (TMA)
 // is ordered after the acquire.

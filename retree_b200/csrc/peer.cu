@@ -26,7 +26,7 @@ namespace {
 
 constexpr int kMaxPeers = 8;
 constexpr int kGatherThreads = 256;
-constexpr uint32_t kPeerWaitLimit = 1u << 22;  // polls x ~100 ns: about half a second
+constexpr uint32_t kPeerWaitLimit = 1u << 22;  // polls (system-scope load + ~100 ns sleep): 0.5 s or more
 
 struct PeerPtrs {
   char* p[kMaxPeers];

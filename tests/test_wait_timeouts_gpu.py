@@ -2,10 +2,10 @@
 
 The peer-memory gather and the gathered projection wait for a flag that
 another rank stores.  Here nothing stores it (one GPU, one process, a flag
-left at zero), so each wait runs out its bound (about half a second), the
-kernel records RT_DEV_WAIT_TIMEOUT in the device status word, skips its
-copies, and exits; the host raises on the status, and the same context keeps
-working -- the calls succeed once the flag is set.
+left at zero), so each wait runs out its bound (4M polls: half a second to
+a few seconds), the kernel records RT_DEV_WAIT_TIMEOUT in the device status
+word, skips its copies, and exits; the host raises on the status, and the
+same context keeps working -- the calls succeed once the flag is set.
 """
 
 import ctypes
