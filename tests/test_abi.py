@@ -212,3 +212,24 @@ def test_launch_switches_without_gpu():
     assert kernels.linear_weight_warm_enabled()
     kernels.set_linear_weight_warm(False)
     assert not kernels.linear_weight_warm_enabled()
+
+
+def test_integration_doc_ctypes_stub_matches_the_library():
+    """The ctypes binding shown in INTEGRATION.md sets argtypes that agree with the header, and its
+    library path is the built one (the stub runs here up to its first device call)."""
+    import ctypes
+
+    doc = (HEADER.parents[1] / "INTEGRATION.md").read_text()
+    blocks = re.findall(r"```python\n(.*?)```", doc, flags=re.S)
+    stub = next(b for b in blocks if "ctypes.CDLL" in b)
+    path = re.search(r'ctypes\.CDLL\("([^"]+)"\)', stub).group(1)
+    assert (HEADER.parents[1] / path).resolve() == _lib.LIB_PATH.resolve()
+    ns: dict = {}
+    exec(compile(stub.replace(path, str(_lib.LIB_PATH)), "INTEGRATION.md", "exec"), ns)
+    lib = ns["lib"]
+    for name in ("rt_kv_compact", "rt_status_string"):
+        res, argtypes = _lib.SIGNATURES[name]
+        assert list(getattr(lib, name).argtypes) == list(argtypes), name
+        assert getattr(lib, name).restype is res, name
+    assert lib.rt_status_string(_lib.RT_ERR_INVALID_ARGUMENT).decode() == "invalid argument"
+    assert callable(ns["compact_tail_inplace"])
