@@ -346,7 +346,7 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
       }
       cluster_sync_all();
       if (epi_warp) {
-        // owned tokens of this round: j = j0, j0 + S, ... (t % S == rank); all
+        // owned tokens of this 32-token pass: j = j0, j0 + S, ... (t % S == rank); all
         // remote loads of a token are issued before any is summed
         const int j0 = ((rank - rnd * 32) % S + S) % S;
         for (int j = j0; j < 32; j += S) {

@@ -215,7 +215,7 @@ def test_launch_switches_without_gpu():
 
 
 def test_integration_doc_ctypes_stub_matches_the_library():
-    """The ctypes binding shown in INTEGRATION.md sets argtypes that agree with the header, and its
+    """The ctypes binding the integration guide shows sets argtypes that agree with the header, and its
     library path is the built one (the stub runs here up to its first device call)."""
     import ctypes
 

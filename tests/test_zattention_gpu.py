@@ -1,6 +1,6 @@
 """GPU parity of tree-verify attention against the fp32 SDPA oracle.
 
-Tolerance (the north-star bound for this path): max |err| <= 2e-2 and
+Tolerance (the bound this path is held to): max |err| <= 2e-2 and
 mean |err| <= 1e-3 against fp32 attention on the same bf16-rounded inputs.
 """
 
