@@ -72,7 +72,8 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="qwen3-4b-b16")
     ap.add_argument("--strategy", default="rank_gated_ngram")
-    ap.add_argument("--cpu-sample-rounds", type=int, default=3)
+    ap.add_argument("--cpu-sample-rounds", type=int, default=24,
+                    help="rounds of the reference path on the host cores for cpu_baseline (N=1 only; ~10 s)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from Python instead of graph replays")
     ap.add_argument("--gemm", choices=("auto", "tcgen05", "cublas"), default="auto",
@@ -243,7 +244,7 @@ def run_reference(args, wl, rank, world):
     value = args.steps / dt
     sample = (f"{args.steps} verify rounds of the reference path on the host CPU (oracle restatement: tree build, "
               f"dense-mask compile, HF sdpa forward bf16, walk, index_select compaction) over a random-KV prefix of "
-              f"{wl['prompt']} tokens")
+              f"{prompt_len(wl, 0)} tokens")
     print(json.dumps({
         "impl": "reference", "metric": "verify rounds/sec", "value": value, "unit": "rounds/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * dt / args.steps, "higher_is_better": True,
@@ -486,15 +487,15 @@ def run_ours(args, wl, rank, world, local_rank):
     hbm_peak, tf_peak, peak_kind = measured_peaks()
     achieved = byts / (attn_us * 1e-6) / 1e9
     traffic = profile_traffic(args.workload)
-    cpu = None
-    if not args.no_cpu_baseline:
+    cpu = None  # the host-core sample runs at N=1 only
+    if not args.no_cpu_baseline and world == 1:
         del v, v2
         torch.cuda.empty_cache()
         rps, secs, cores = cpu_round_sample(cfg, wl, args.cpu_sample_rounds, args.strategy)
         cpu = {"value": rps, "unit": "rounds/s", "cores": cores, "kind": "port",
                "sample": (f"{args.cpu_sample_rounds} verify rounds ({secs:.1f} s) of the reference path on the host "
                           f"CPU: oracle tree build, dense-mask compile, HF sdpa forward (bf16), walk, compaction, "
-                          f"random-KV prefix of {wl['prompt']} tokens")}
+                          f"random-KV prefix of {prompt_len(wl, 0)} tokens")}
     reqs = 1 if wl.get("split") else world  # a split request is one request over all ranks
     value = reqs * steps / dev_s
     split_exchange = dict(nccl="NCCL", p2p="peer memory", p2p_fused="peer memory, pulled by o_proj")[args.exchange]
