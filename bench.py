@@ -29,7 +29,6 @@ import argparse
 import datetime
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -95,8 +94,9 @@ def parse():
                          "seeded recovery memory, instead of the exact walk")
     ap.add_argument("--dp-exchange", choices=("nccl", "p2p"), default="nccl",
                     help="request DP at N>1: the per-step recovery-delta all-gather over NCCL or over peer memory")
-    ap.add_argument("--pdl", choices=("auto", "on", "off"), default="auto",
-                    help="programmatic dependent launch (auto: on at N=1, off when NCCL runs beside the kernels)")
+    ap.add_argument("--pdl", choices=("auto", "off"), default="auto",
+                    help="programmatic dependent launch at N=1 (auto: on); always off at N>1, where NCCL runs "
+                         "beside the kernels")
     ap.add_argument("--exchange", choices=("nccl", "p2p", "p2p_fused"), default="nccl",
                     help="split workloads: attention-output all-gather over NCCL or over peer memory")
     return ap.parse_args()
@@ -116,13 +116,22 @@ def measured_peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-def profile_traffic(workload: str):
-    """DRAM bytes per attention launch from the committed ncu summary, if present."""
-    path = os.path.join(ROOT, "profiles", "tree_attn_ncu.md")
-    if not os.path.exists(path):
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one tree-attention launch, from an ncu capture
+# of the current kernel at the workload's live shape: workload -> (bytes, prefix_len, tree_nodes, how taken).
+# Scaled to the live prefix by the K/V bytes per key when the bench's prefix differs.
+ATTN_TRAFFIC = {}
+
+
+def attn_traffic(workload: str, prefix_len: int, n_tree: int, hkv: int):
+    """The ncu-measured DRAM traffic of one attention launch at this workload, or None when not captured."""
+    rec = ATTN_TRAFFIC.get(workload)
+    if rec is None or rec[2] != n_tree:
         return None
-    m = re.search(rf"traffic_bytes_per_launch\[{re.escape(workload)}\]:\s*([0-9.eE+]+)", open(path).read())
-    return float(m.group(1)) if m else None
+    byts, L, n, how = rec
+    per_key = 2 * hkv * 128 * 2
+    scaled = byts + (prefix_len - L) * per_key
+    return {"bytes": scaled, "source": f"{how}; captured at prefix {L}, scaled to {prefix_len} at {per_key} B per key"
+            if prefix_len != L else how}
 
 
 CLOCK_QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
@@ -415,14 +424,14 @@ def run_ours(args, wl, rank, world, local_rank):
         hq, hkv = hq // world, hkv // world
     q_probe = torch.randn((1, hq, n_tree, 128), device=dev, dtype=torch.bfloat16)
     bits = v.tree["mask"][:n_tree].clone()
-    plen = torch.tensor([L_live], dtype=torch.int64, device=dev)
+    live_len_dev = torch.tensor([L_live], dtype=torch.int64, device=dev)
     splits = kernels.default_splits(n_tree, hq, hkv, cap - n_tree)
     out_probe = torch.empty((n_tree, hq, 128), device=dev, dtype=torch.bfloat16)
 
     def attn_all_layers():
         for li in range(cfg.num_hidden_layers):
             kernels.tree_attention(q_probe, v.cache.slab[2 * li], v.cache.slab[2 * li + 1], bits, cap - n_tree,
-                                   out=out_probe, prefix_len_dev=plen, kv_capacity=cap, num_splits=splits)
+                                   out=out_probe, prefix_len_dev=live_len_dev, kv_capacity=cap, num_splits=splits)
 
     attn_all_layers()
     side = torch.cuda.Stream(dev)
@@ -484,9 +493,7 @@ def run_ours(args, wl, rank, world, local_rank):
         delta_peer.close()
     if rank != 0:
         return
-    hbm_peak, tf_peak, peak_kind = measured_peaks()
-    achieved = byts / (attn_us * 1e-6) / 1e9
-    traffic = profile_traffic(args.workload)
+    traffic = attn_traffic(args.workload, L_live, n_tree, hkv)
     cpu = None  # the host-core sample runs at N=1 only
     if not args.no_cpu_baseline and world == 1:
         del v, v2
@@ -497,16 +504,45 @@ def run_ours(args, wl, rank, world, local_rank):
                           f"CPU: oracle tree build, dense-mask compile, HF sdpa forward (bf16), walk, compaction, "
                           f"random-KV prefix of {prompt_len(wl, 0)} tokens")}
     reqs = 1 if wl.get("split") else world  # a split request is one request over all ranks
-    value = reqs * steps / dev_s
+    print(result_line(args, wl, world=world, reqs=reqs, steps=steps, warm=warm, dev_s=dev_s, e2e_s=e2e_s,
+                      wall=wall, prompt=plen, projections=projections, pdl=kernels.pdl_enabled(),
+                      accepted=accepted, attn_us=attn_us, byts=byts, prefix_len=L_live, n_tree=n_tree,
+                      splits=splits, layers=cfg.num_hidden_layers, traffic=traffic, cpu=cpu, h2d=h2d, d2h=d2h,
+                      launches=launches, clocks=clocks), flush=True)
+
+
+def plain(x):
+    """``x`` with tensors and numpy values turned into Python numbers and lists (JSON-serialisable)."""
+    if isinstance(x, torch.Tensor):
+        x = x.detach().cpu()
+        return x.item() if x.numel() == 1 else x.tolist()
+    if isinstance(x, np.ndarray):
+        return x.tolist()
+    if isinstance(x, np.generic):
+        return x.item()
+    if isinstance(x, dict):
+        return {str(k): plain(v) for k, v in x.items()}
+    if isinstance(x, (list, tuple)):
+        return [plain(v) for v in x]
+    return x
+
+
+def result_line(args, wl, *, world, reqs, steps, warm, dev_s, e2e_s, wall, prompt, projections, pdl, accepted,
+                attn_us, byts, prefix_len, n_tree, splits, layers, traffic, cpu, h2d, d2h, launches, clocks) -> str:
+    """The bench's JSON line from the measured quantities (any of which may be a 1-element tensor)."""
+    dev_s, e2e_s, attn_us, byts = (float(plain(x)) for x in (dev_s, e2e_s, attn_us, byts))
+    hbm_peak, _, peak_kind = measured_peaks()
+    achieved = byts / (attn_us * 1e-6) / 1e9
     split_exchange = dict(nccl="NCCL", p2p="peer memory", p2p_fused="peer memory, pulled by o_proj")[args.exchange]
     dp_exchange = "peer memory" if args.dp_exchange == "p2p" else "NCCL"
-    print(json.dumps({
-        "metric": "verify rounds/sec", "value": value, "unit": "rounds/s", "n_gpus": world, "steps": steps,
-        "warmup": warm, "ms_per_step": 1000.0 * dev_s / steps, "higher_is_better": True,
+    accepted = [plain(a) for a in accepted]
+    line = {
+        "metric": "verify rounds/sec", "value": reqs * steps / dev_s, "unit": "rounds/s", "n_gpus": world,
+        "steps": steps, "warmup": warm, "ms_per_step": 1000.0 * dev_s / steps, "higher_is_better": True,
         "scaling": "strong" if wl.get("split") else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded draft logits, uniform prompt, random-init "
                                                       "weights)",
-        "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": plen,
+        "config": {"workload": args.workload, "model": wl["model"] + " (random init)", "prompt": prompt,
                    "prompt_lengths": [prompt_len(wl, 0 if wl.get("split") else r) for r in range(world)],
                    "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
@@ -519,20 +555,23 @@ def run_ours(args, wl, rank, world, local_rank):
                                    f"{split_exchange})" if wl.get("split") else
                                    f"dp{world} (one request per GPU)" + (
                                        f", recovery-delta all-gather per step ({dp_exchange})" if world > 1 else "")),
-                   "pdl": kernels.pdl_enabled(),
+                   "pdl": pdl,
                    "l2": "inputs > L2 (8 GB of weights and the KV cache stream every round)",
-                   "mean_accepted": sum(accepted) / len(accepted), "wall_s": wall},
-        "roofline": {"kernel": "tree_attn (rt_tree_attn + split combine)", "bound": "hbm", "achieved": achieved,
-                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak, "traffic": traffic,
+                   "mean_accepted": sum(accepted) / max(1, len(accepted)), "wall_s": wall},
+        "roofline": {"kernel": "tree_attn (rt_tree_attn)", "bound": "hbm", "achieved": achieved,
+                     "peak": hbm_peak, "unit": "GB/s", "frac": achieved / hbm_peak,
+                     "traffic": None if traffic is None else traffic["bytes"],
+                     "traffic_source": None if traffic is None else traffic["source"],
                      "peak_kind": peak_kind, "avg_launch_us": attn_us, "algorithmic_bytes_per_launch": byts,
-                     "prefix_len": L_live, "tree_nodes": n_tree, "key_splits": splits,
-                     "share_of_round": cfg.num_hidden_layers * attn_us * 1e-3 / (1000.0 * dev_s / steps)},
+                     "prefix_len": prefix_len, "tree_nodes": n_tree, "key_splits": splits,
+                     "share_of_round": layers * attn_us * 1e-3 / (1000.0 * dev_s / steps)},
         "cpu_baseline": cpu,
         "e2e": {"value": reqs * steps / e2e_s, "unit": "rounds/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,
         "clocks": clocks,
-    }), flush=True)
+    }
+    return json.dumps(plain(line))
 
 
 def main():
@@ -548,19 +587,18 @@ def main():
         import torch.distributed as dist
         # the per-step exchanges are tiny all-gathers: no NVLink multicast objects needed
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        # no programmatic dependent launch next to NCCL streams (rt_set_pdl), from the first launch on,
-        # unless asked for (--pdl on)
-        os.environ["RETREE_B200_PDL"] = "1" if args.pdl == "on" else "0"
+        # no programmatic dependent launch in a process with NCCL collectives, from the first launch on
+        os.environ["RETREE_B200_PDL"] = "0"
 
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
         from retree_b200 import kernels
-        kernels.set_pdl(args.pdl == "on")  # NCCL collectives share the stream with the forward's kernels
+        kernels.set_pdl(False)  # NCCL collectives run between the forward's kernels
         log(rank, "process group up")
-    elif args.pdl != "auto":
+    elif args.pdl == "off":
         from retree_b200 import kernels
-        kernels.set_pdl(args.pdl == "on")
+        kernels.set_pdl(False)
     try:
         run_ours(args, wl, rank, world, local_rank)
     finally:

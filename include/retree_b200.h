@@ -230,7 +230,10 @@ int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_
  * library until the process exits.  A shape whose rt_tree_attn_workspace_size
  * exceeds it returns RT_ERR_WORKSPACE.  The first call on a device looks the
  * array's address up for that device (that device must be current), so it
- * must come before any stream capture.  Every call shares the one array:
+ * must come before any stream capture.  The looked-up address is kept for
+ * the life of the process: after cudaDeviceReset (or anything else that
+ * destroys the device's primary context) it is stale, and this entry point
+ * must not be called on that device again.  Every call shares the one array:
  * calls that overlap on the GPU race on it.
  * ---------------------------------------------------------------------- */
 size_t rt_tree_attn_noalloc_max_bytes(void);

@@ -156,8 +156,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // written while the round's forward runs (only rows from prefix_len on, by
   // this layer's projection), so the producer requests the leading pure-prefix
   // K/V blocks before waiting for the previous kernel; Q, the tree block, the
-  // mask and every write come after the wait.
-  pdl_launch_dependents();
+  // mask and every write come after the wait.  Dependents are released only
+  // once this CTA holds its TMEM columns (below): a dependent CTA on the same
+  // SM that allocated first and then waited for this grid would otherwise
+  // leave this CTA's allocation waiting for columns that never free.
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x, kvh = blockIdx.y, mt = blockIdx.z;
   const int G = p.group;
@@ -227,6 +229,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_launch_dependents();
   const uint32_t tmem = bar.tmem_base;
   volatile int* abort_flag = &bar.abort_flag;
 
@@ -945,7 +948,9 @@ extern "C" int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_
 //
 // Its device address is looked up once per device (cudaGetSymbolAddress with
 // that device current) on the first call on that device, so that first call
-// must not be made while a stream is being captured.  All calls share the one
+// must not be made while a stream is being captured.  The address is kept for
+// the life of the process; a device reset (cudaDeviceReset, or a destroyed
+// primary context) leaves it stale.  All calls share the one
 // array: calls whose launches overlap on the GPU (different streams, or
 // different host threads) race on it.  Nothing in it has to start at zero --
 // every split writes all of its partial rows (or its neutral -inf/0 row)

@@ -122,6 +122,7 @@ class FusedTarget:
         cfg = model.config
         inner = model.model
         dev = next(model.parameters()).device
+        kernels.pdl_guard()  # no dependent launch beside NCCL collectives
         self.device = dev
         self.cache = cache
         self.n_max = int(n_max)

@@ -73,9 +73,27 @@ def _count(n: int = 1) -> None:
     LAUNCHES += n
 
 
+def _nccl_group_up() -> bool:
+    import torch.distributed as dist
+    return dist.is_available() and dist.is_initialized() and dist.get_backend() == "nccl"
+
+
 def set_pdl(enabled: bool) -> None:
-    """Programmatic dependent launch between the verify-forward kernels (off under NCCL; see rt_set_pdl)."""
+    """Programmatic dependent launch between the verify-forward kernels (rt_set_pdl).
+
+    It is never turned on in a process with an NCCL process group: a 2-process
+    run with NCCL collectives between dependent-launched kernels stalled, with
+    no cause found, so the two are kept apart (``pdl_guard``).
+    """
+    if enabled and _nccl_group_up():
+        raise RuntimeError("programmatic dependent launch stays off in a process with an NCCL process group")
     _lib.load().rt_set_pdl(int(bool(enabled)))
+
+
+def pdl_guard() -> None:
+    """Turn programmatic dependent launch off if this process has an NCCL process group."""
+    if _nccl_group_up():
+        _lib.load().rt_set_pdl(0)
 
 
 def pdl_enabled() -> bool:

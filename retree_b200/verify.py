@@ -66,6 +66,7 @@ class TreeVerifier:
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
         self.target = target
         self.device = torch.device(device) if device is not None else next(target.parameters()).device
+        kernels.pdl_guard()  # no dependent launch beside NCCL collectives
         self.budget = max(int(tree_budget), 0)
         self.horizon = int(draft_horizon)
         self.temperature = float(temperature)

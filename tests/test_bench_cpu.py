@@ -1,62 +1,60 @@
-"""bench.py's JSON contract on the CPU: the reference arm (the reference's round on the host cores)
-prints one line with the contract's keys, and the workload helpers behave."""
+"""bench.py's JSON line: assembled from measured values that may still be tensors, it must serialise."""
 
 import json
-import subprocess
 import sys
-from pathlib import Path
+
+import torch
 
 import bench
 
-ROOT = Path(__file__).resolve().parents[1]
+
+def _args(argv=()):
+    old = sys.argv
+    sys.argv = ["bench.py", *argv]
+    try:
+        return bench.parse()
+    finally:
+        sys.argv = old
 
 
-def test_reference_arm_prints_one_contract_line():
-    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0"],
-                       cwd=ROOT, capture_output=True, text=True, timeout=900)
-    assert r.returncode == 0, r.stderr[-2000:]
-    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
-    assert len(lines) == 1
-    d = json.loads(lines[0])
-    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better",
-                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e", "impl"):
-        assert key in d, key
-    assert d["impl"] == "reference" and d["metric"] == "verify rounds/sec" and d["value"] > 0
-    assert d["cpu_baseline"]["cores"] >= 1 and d["cpu_baseline"]["kind"] in ("port", "reference")
-    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
-    assert d["config"]["workload"] == "qwen3-4b-b16"
+def test_result_line_serialises_tensor_and_plain_inputs():
+    args = _args()
+    wl = bench.WORKLOADS[args.workload]
+    line = bench.result_line(
+        args, wl, world=1, reqs=1, steps=20, warm=5, dev_s=torch.tensor([0.066], dtype=torch.float64),
+        e2e_s=0.07, wall=0.08, prompt=2048, projections={"qkv": "rt_linear"}, pdl=True,
+        accepted=[torch.tensor(1), 2, 1], attn_us=torch.tensor(4.5), byts=8_853_572, prefix_len=torch.tensor([2075]),
+        n_tree=17, splits=8, layers=36, traffic={"bytes": 8.9e6, "source": "ncu"}, cpu=None, h2d=4_558_080, d2h=148,
+        launches=4000, clocks={"sm_mhz": 1965.0, "sm_max_mhz": 1965.0, "reasons": []})
+    d = json.loads(line)
+    assert d["metric"] == "verify rounds/sec" and d["unit"] == "rounds/s"
+    assert abs(d["value"] - 20 / 0.066) < 1e-6
+    assert d["config"]["prompt"] == 2048 and d["roofline"]["prefix_len"] == 2075
+    assert d["roofline"]["traffic"] == 8.9e6 and d["roofline"]["bound"] == "hbm"
+    assert 0 < d["roofline"]["frac"] < 10
+    assert d["e2e"]["h2d_bytes_per_step"] == 4_558_080
+    assert d["config"]["mean_accepted"] == 4 / 3
 
 
-def test_workload_prompt_lengths():
-    assert bench.prompt_len(bench.WORKLOADS["qwen3-4b-b16"], 5) == 2048
-    lens = [bench.prompt_len(bench.WORKLOADS["qwen3-8b-b64"], r) for r in range(8)]
-    assert all(1024 <= x <= 8192 for x in lens) and len(set(lens)) > 1
-    assert lens == [bench.prompt_len(bench.WORKLOADS["qwen3-8b-b64"], r) for r in range(8)]  # seeded
+def test_pdl_cannot_be_forced_on():
+    """The bench has no switch that turns programmatic dependent launch on (it is on by default at N=1 only)."""
+    assert _args(["--pdl", "off"]).pdl == "off"
+    try:
+        _args(["--pdl", "on"])
+    except SystemExit:
+        pass
+    else:
+        raise AssertionError("--pdl on must not parse")
 
 
-def test_clock_summary_uses_samples_of_the_timed_region():
-    import datetime
-
-    def row(t, sm, *reasons):
-        ts = datetime.datetime.fromtimestamp(t).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
-        act = ["Active" if r else "Not Active" for r in reasons]
-        return f"{ts}, 0, {sm}, 1965, 900.0, 0x0, {act[0]}, {act[1]}, {act[2]}, {act[3]}"
-
-    t0 = 1_800_000_000.0
-    lines = [row(t0 - 1.0, 800, 0, 0, 0, 0),            # idle, before the region
-             row(t0 + 0.01, 1965, 0, 0, 0, 1), row(t0 + 0.03, 1950, 0, 0, 0, 1),
-             row(t0 + 2.0, 700, 1, 0, 0, 0), "garbage"]   # after it
-    d = bench.summarize_clocks(lines, t0, t0 + 0.04, 0.02)
-    assert d["samples_in_region"] == 2 and d["sm_mhz"] == 1957.5 and d["sm_max_mhz"] == 1965.0
-    assert d["reasons"] == ["sw_power_cap"]
-    # no sample inside: the nearest one stands in
-    d = bench.summarize_clocks(lines[:1], t0, t0 + 0.04, 0.02)
-    assert d["samples_in_region"] == 0 and d["sm_mhz"] == 800
-    assert bench.summarize_clocks([], t0, t0, 0.02)["reasons"] == ["no samples"]
-
-
-def test_clock_summary_without_readable_timestamps_uses_every_sample():
-    lines = ["Tue Dec 1 00:00:00 2026, 0, 1900, 1965, 800.0, 0x0, Not Active, Not Active, Not Active, Active",
-             "Tue Dec 1 00:00:01 2026, 0, 1800, 1965, 800.0, 0x0, Not Active, Not Active, Not Active, Not Active"]
-    d = bench.summarize_clocks(lines, 0.0, 1.0, 0.02)
-    assert d["sm_mhz"] == 1850 and d["reasons"] == ["sw_power_cap"] and d["samples"] == 2
+def test_attn_traffic_scales_with_the_live_prefix():
+    old = dict(bench.ATTN_TRAFFIC)
+    try:
+        bench.ATTN_TRAFFIC["w"] = (1_000_000, 2000, 17, "ncu capture")
+        assert bench.attn_traffic("w", 2000, 17, 8)["bytes"] == 1_000_000
+        assert bench.attn_traffic("w", 2010, 17, 8)["bytes"] == 1_000_000 + 10 * 4096
+        assert bench.attn_traffic("w", 2010, 65, 8) is None
+        assert bench.attn_traffic("other", 2010, 17, 8) is None
+    finally:
+        bench.ATTN_TRAFFIC.clear()
+        bench.ATTN_TRAFFIC.update(old)

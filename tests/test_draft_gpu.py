@@ -4,8 +4,10 @@
 pinned to the reference's module by tests/golden/dflash.npz) in fp32 on the
 same bf16-rounded weights and inputs, over consecutive calls that share the
 draft cache (first call over a whole prompt's context rows, then decode-sized
-calls).  Tolerance: relative L2 error below 2e-2 (bf16 activations through
-the layers) and below 1e-2 against the same restatement run in bf16.
+calls).  Tolerance, against the fp32 restatement: relative L2 error below 2e-2
+(bf16 activations through the layers), and no more than twice the error of
+the draft module's own bf16 forward on the same inputs (both round to bf16 at
+every stage, in different orders: neither is the reference for the other).
 
 The fused verify forward's layer outputs (the draft's context features,
 HF ``hidden_states[i + 1]``) are compared with the HF forward's, and
@@ -76,8 +78,11 @@ def test_fused_draft_matches_restated_forward(ctx_chunk):
     want32 = od.run_calls(ref32, [(th.float(), e.float()) for th, e in seq], device=dev, dtype=torch.float32)
     want16 = od.run_calls(ref16, seq, device=dev, dtype=torch.bfloat16)
     for j in range(len(calls)):
-        assert _rel(got[j], want32[j]) < 2e-2, (j, _rel(got[j], want32[j]))
-        assert _rel(got[j], want16[j]) < 1e-2, (j, _rel(got[j], want16[j]))
+        e_got, e_mod = _rel(got[j], want32[j]), _rel(want16[j], want32[j])
+        print(f"call {j}: fused vs fp32 {e_got:.5f}, bf16 module vs fp32 {e_mod:.5f}, "
+              f"fused vs bf16 module {_rel(got[j], want16[j]):.5f}")
+        assert e_got < 2e-2, (j, e_got)
+        assert e_got <= max(2.0 * e_mod, 5e-3), (j, e_got, e_mod)
     # crop semantics: the block's rows are not kept, so the same block at the
     # same start (no new context) gives the same output
     th, ids = calls[-1]

@@ -67,6 +67,19 @@ def test_noalloc_matches_workspace_entry_point_twice():
         assert int(status.item()) == 0
         err = (got.float() - want.float()).abs()
         assert float(err.max()) <= MAX_ABS and float(err.mean()) <= MEAN_ABS
-    # a shape whose partials exceed the fixed array is refused, not truncated
-    big_need = lib.rt_tree_attn_workspace_size(1025, 32, 8, 128, 1 << 20, 64)
-    assert big_need > lib.rt_tree_attn_noalloc_max_bytes()
+    # a shape whose partials exceed the fixed array is refused before any launch:
+    # RT_ERR_WORKSPACE, the output left as it was and no device status raised
+    n_big, prefix_big, splits_big = 257, 4096, 64
+    assert lib.rt_tree_attn_workspace_size(n_big, 32, 8, 128, prefix_big, splits_big) > \
+        lib.rt_tree_attn_noalloc_max_bytes()
+    q, k, v, bits = _case(3, n_big, prefix_big, dev)
+    out = torch.full_like(q, float("nan"))
+    torch.cuda.synchronize()
+    rc = lib.rt_tree_attn_noalloc(q.data_ptr(), q.stride(0) * 2, q.stride(1) * 2, k.data_ptr(), v.data_ptr(),
+                                  k.stride(0) * 2, k.stride(1) * 2, k.shape[1], out.data_ptr(), out.stride(0) * 2,
+                                  out.stride(1) * 2, bits.data_ptr(), bits.shape[1], n_big, prefix_big, None, 32, 8,
+                                  128, ctypes.c_float(128 ** -0.5), splits_big, 0, status.data_ptr(), stream)
+    assert rc == _lib.RT_ERR_WORKSPACE, _lib.status_string(rc)
+    torch.cuda.synchronize()
+    assert bool(torch.isnan(out.float()).all())
+    assert int(status.item()) == 0
