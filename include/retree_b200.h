@@ -130,9 +130,13 @@ int rt_kv_append(void* k_cache, void* v_cache, int64_t cache_head_stride, int64_
  * prefix_len is read from prefix_len_dev (int64, DEVICE) when non-NULL; then
  * prefix_len is only an upper bound used to size the launch.
  *
- * Keys are split into num_splits ranges (0 = choose) whose partial results
- * are merged by a second kernel; workspace must hold
- * rt_tree_attn_workspace_size(...) bytes (alignment 256).  Requires
+ * Keys are split into num_splits ranges (0 = choose).  On the tcgen05 path
+ * the ranges of one (kv head, 128-row tile) run as one thread-block cluster
+ * (2..16 CTAs, when every cluster of the launch fits on the GPU at once) and
+ * are merged inside the kernel through distributed shared memory; otherwise
+ * their partial results go through the workspace to a second kernel.
+ * workspace must hold rt_tree_attn_workspace_size(...) bytes (alignment 256;
+ * rt_tree_attn_plan says whether a launch uses it).  Requires
  * num_q_heads % num_kv_heads == 0, head_dim == 128, all strides multiples of
  * 16 bytes, q/k/v/out 16-byte aligned.  n * (num_q_heads/num_kv_heads) >= 64
  * runs on tcgen05 (TMEM accumulators, TMA-fed K/V); smaller trees run a
@@ -215,6 +219,14 @@ int rt_peer_gather(void* const* peer_bufs, int world, int rows, int64_t row_byte
 
 /* Number of key splits rt_tree_attn chooses for this shape (num_splits = 0). */
 int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len);
+
+/* How rt_tree_attn runs a shape (no counterpart in the reference; a query
+ * for hosts that size buffers or count launches): *splits_out = key splits,
+ * *merged_out = 1 when they are merged inside the kernel (one launch, no
+ * workspace) and 0 when a workspace and a second (combine) launch are used,
+ * *tcgen05_out = 1 on the tcgen05 path.  Outputs may be NULL. */
+int rt_tree_attn_plan(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len, int num_splits, int path,
+                      int* splits_out, int* merged_out, int* tcgen05_out);
 
 /* ------------------------------------------------------------------------
  * Tree-verify attention that allocates nothing.

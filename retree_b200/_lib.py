@@ -37,6 +37,7 @@ SIGNATURES = {
     "rt_tree_attn_ex": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                              _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P, _P]),
     "rt_tree_attn_default_splits": (_I, [_I, _I, _I, _I64]),
+    "rt_tree_attn_plan": (_I, [_I, _I, _I, _I64, _I, _I, _P, _P, _P]),
     "rt_l2_prefetch": (_I, [_P, _I, _P]),
     "rt_ipc_alloc": (_I, [_SZ, _P, _P]),
     "rt_ipc_free": (_I, [_P]),

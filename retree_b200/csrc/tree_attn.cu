@@ -51,6 +51,13 @@ constexpr uint32_t kOffV = 3 * kTile;       // 2 stages
 constexpr uint32_t kOffP = 5 * kTile;       // 2 buffers
 constexpr uint32_t kOffBar = 7 * kTile;
 constexpr uint32_t kAttnSmem = kOffBar + 1536 + 1024;  // + barriers/exchange + alignment slack
+// In-kernel split merge: once a CTA's last PV product is final, the Q / K / V
+// ring is idle and holds the CTA's unnormalised fp32 O tile (rows of 512 B,
+// 16-byte chunks XOR-swizzled by row) and its rows' (m, l).
+constexpr uint32_t kOffStage = 0;
+constexpr uint32_t kOffMl = 2 * kTile;
+constexpr uint32_t kOffWeights = 3 * kTile;  // [owned rows][kMaxMerge] fp32 merge weights
+constexpr int kMaxMerge = 16;  // cluster size limit (16 needs the non-portable cluster attribute)
 constexpr uint32_t kTmemCols = 512;                   // S0 | S1 | O | spare
 constexpr float kRescaleThreshold = 8.0f;             // log2 units
 
@@ -65,6 +72,7 @@ struct AttnParams {
   int64_t prefix_len;
   const int64_t* prefix_len_dev;
   int group, num_kv_heads, tiles, num_splits;
+  int merge;       // 1: the splits of a (kv head, tile) form one cluster and are merged in the kernel
   float scale_log2;
   float* ws_o;     // [split][kv_head][tiles*128][128]
   float2* ws_ml;   // [split][kv_head][tiles*128]  (m in log2 units, l)
@@ -88,13 +96,13 @@ __device__ __forceinline__ int64_t key_count(const AttnParams& p) {
   return L + p.n;
 }
 
-// Block range [b0, b1) of this split.
+// Block range [b0, b1) of this split: the blocks spread evenly (range sizes
+// differ by at most one, so no split runs two blocks while another idles).
 __device__ __forceinline__ void split_range(int64_t total_keys, int split, int splits, int64_t blk, int64_t& b0,
                                             int64_t& b1) {
   const int64_t nblk = (total_keys + blk - 1) / blk;
-  const int64_t per = (nblk + splits - 1) / splits;
-  b0 = min(nblk, split * per);
-  b1 = min(nblk, b0 + per);
+  b0 = nblk * split / splits;
+  b1 = nblk * (split + 1) / splits;
 }
 
 __device__ __forceinline__ void write_neutral_partial(const AttnParams& p, int split, int kvh, int row0, int rows) {
@@ -137,6 +145,99 @@ __device__ __forceinline__ uint32_t visible_word(int64_t k0, int64_t L, int n, c
   return bits | tb;
 }
 
+__device__ __forceinline__ float2 ld_cluster_f32x2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ float4 ld_cluster_f32x4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+// Byte offset of 16-byte chunk `c` (0..31) of row `r` in the merge's O stage.
+__device__ __forceinline__ uint32_t stage_off(int r, int c) {
+  return kOffStage + static_cast<uint32_t>(r) * 512u + static_cast<uint32_t>((c ^ (r & 31)) << 4);
+}
+
+// The split merge inside the cluster (every thread of every CTA calls it; the
+// cluster is the S = num_splits CTAs of one (kv head, tile), rank = split).
+// Each CTA has staged its unnormalised O rows and (m, l) in its own shared
+// memory.  Rank c merges the tile rows r = c, c + S, ...: first one thread per
+// row reads every rank's (m, l) and keeps the rank weights 2^(m_s - M) / L
+// (L = sum_s 2^(m_s - M) l_s, in rank order) in shared memory; then one thread
+// per (row, 4-dim chunk) reads every rank's chunk -- all loads in flight at
+// once -- and sums them in rank order (a rank of weight 0 is skipped, never
+// multiplied) into the bf16 output.  The last barrier keeps every CTA's
+// shared memory until all ranks have read it.
+__device__ __forceinline__ void merge_splits(const AttnParams& p, unsigned char* smem, int rank, int kvh, int row0,
+                                             int rows_total) {
+  __syncwarp();
+  cluster_sync_all();
+  const int tid = threadIdx.x;
+  const int S = p.num_splits, G = p.group;
+  const int rows_here = min(kBM, rows_total - row0);
+  const int owned = rows_here > rank ? (rows_here - rank + S - 1) / S : 0;
+  const uint32_t base = smem_u32(smem);
+  float* wtab = reinterpret_cast<float*>(smem + kOffWeights);
+  for (int i = tid; i < owned; i += kAttnThreads) {
+    const int rr = rank + S * i;
+    float2 ml[kMaxMerge];
+#pragma unroll
+    for (int u = 0; u < kMaxMerge; ++u)
+      ml[u] = u < S ? ld_cluster_f32x2(cluster_map(base + kOffMl + rr * 8, u)) : make_float2(-INFINITY, 0.f);
+    float M = -INFINITY;
+#pragma unroll
+    for (int u = 0; u < kMaxMerge; ++u) M = fmaxf(M, ml[u].x);
+    float w[kMaxMerge];
+    float lsum = 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxMerge; ++u) {
+      w[u] = (M == -INFINITY || ml[u].x == -INFINITY) ? 0.f : ex2(ml[u].x - M);
+      lsum = fmaf(w[u], ml[u].y, lsum);
+    }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+    for (int u = 0; u < kMaxMerge; ++u) wtab[i * kMaxMerge + u] = w[u] * inv;
+  }
+  __syncthreads();
+  for (int it = tid; it < owned * 32; it += kAttnThreads) {
+    const int i = it >> 5, c = it & 31;
+    const int rr = rank + S * i;
+    const uint32_t off = base + stage_off(rr, c);
+    float wu[kMaxMerge];
+    float4 o[kMaxMerge];
+#pragma unroll
+    for (int u = 0; u < kMaxMerge; ++u) {
+      wu[u] = wtab[i * kMaxMerge + u];
+      o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (u < S && wu[u] != 0.f) o[u] = ld_cluster_f32x4(cluster_map(off, u));
+    }
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int u = 0; u < kMaxMerge; ++u) {
+      if (u < S && wu[u] != 0.f) {
+        acc.x = fmaf(wu[u], o[u].x, acc.x);
+        acc.y = fmaf(wu[u], o[u].y, acc.y);
+        acc.z = fmaf(wu[u], o[u].z, acc.z);
+        acc.w = fmaf(wu[u], o[u].w, acc.w);
+      }
+    }
+    const int R = row0 + rr;
+    const int node = R / G, h = kvh * G + (R - node * G);
+    uint2 pk;
+    pk.x = pack_bf16x2(acc.x, acc.y);
+    pk.y = pack_bf16x2(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(p.out + node * p.out_tok_stride + h * p.out_head_stride + c * 8) = pk;
+  }
+  __syncwarp();
+  cluster_sync_all();
+}
+
 __device__ __forceinline__ uint32_t ex2_f16x2(float lo, float hi) {
   uint32_t h, e;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
@@ -173,6 +274,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const int nb = static_cast<int>(b1 - b0);
   if (nb <= 0) {
     pdl_wait();
+    if (p.merge > 1) {
+      // no keys here: neutral (m, l) for every row, then this rank's share of the merge
+      float2* ml = reinterpret_cast<float2*>(smem + kOffMl);
+      for (int r = tid; r < kBM; r += kAttnThreads) ml[r] = make_float2(-INFINITY, 0.f);
+      __syncthreads();
+      merge_splits(p, smem, split, kvh, row0, rows_total);
+      return;
+    }
     if (p.num_splits > 1) write_neutral_partial(p, split, kvh, row0, min(kBM, rows_total - row0));
     return;
   }
@@ -180,7 +289,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   int pre = 0;
   while (pre < min(2, nb) && (b0 + pre + 1) * kBN <= L) ++pre;
 
-  if (tid == 0) {
+  // The producer lane sets up the barriers and sends the pure-prefix K/V loads
+  // out at once, while the MMA warp allocates TMEM (nothing before the block
+  // barrier below waits for another warp).
+  const bool kv_hint = p.pf.count > 0;  // evict-first K/V loads while an L2 warm-up is in flight
+  const uint64_t kv_policy = kv_hint ? l2_policy_evict_first() : 0ull;
+  auto load_kv = [&](uint64_t* full, const CUtensorMap* map, unsigned char* dst, int key0) {
+    mbar_arrive_expect_tx(full, kTile);
+    if (kv_hint) {
+      tma_load_3d_hint(dst, map, full, 0, key0, kvh, kv_policy);
+      tma_load_3d_hint(dst + kHalf, map, full, 64, key0, kvh, kv_policy);
+    } else {
+      tma_load_3d(dst, map, full, 0, key0, kvh);
+      tma_load_3d(dst + kHalf, map, full, 64, key0, kvh);
+    }
+  };
+  if (warp == kProducerWarp && lane == 0) {
+    prefetch_tmap(&tmap_k);
+    prefetch_tmap(&tmap_v);
+    if (q_tma) prefetch_tmap(&tmap_q);
     mbar_init(&bar.full_q, 1);
     for (int i = 0; i < 2; ++i) {
       mbar_init(&bar.full_k[i], 1);
@@ -195,6 +322,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(&bar.fin, 1);
     bar.abort_flag = 0;
     fence_mbar_init();
+    fence_proxy_async_smem();
+    for (int j = 0; j < pre; ++j) {
+      const int key0 = static_cast<int>((b0 + j) * kBN);
+      load_kv(&bar.full_k[j], &tmap_k, smem + kOffK + j * kTile, key0);
+      load_kv(&bar.full_v[j], &tmap_v, smem + kOffV + j * kTile, key0);
+    }
   }
   if (warp == kMmaWarp) {
     tmem_alloc(&bar.tmem_base, kTmemCols);
@@ -235,10 +368,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (warp == kProducerWarp) {
     // ---------------- TMA producer: lane 0 Q and K, lane 1 V ----------------
-    // with an L2 warm-up in flight the K/V stream (read once per round) is
-    // loaded evict-first, so it does not push the warmed lines out
-    const bool kv_hint = p.pf.count > 0;
-    const uint64_t kv_policy = kv_hint ? l2_policy_evict_first() : 0ull;
+    // (the first `pre` K and V blocks went out in the prologue)
     if (lane == 0) {
       auto issue_q = [&] {
         pdl_wait();
@@ -251,10 +381,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mbar_arrive(&bar.full_q);
         }
       };
-      if (q_tma) prefetch_tmap(&tmap_q);
-      int issued = 0;
+      int issued = pre;
       bool q_issued = false;
-      for (int j = 0; j < nb; ++j) {
+      for (int j = pre; j < nb; ++j) {
         if (j == pre) {
           issue_q();
           q_issued = true;
@@ -262,16 +391,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int st = j & 1;
         // stage st is free once S(j-2) has consumed it
         if (!mbar_wait(&bar.empty_k[st], ((j >> 1) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
-        const int key0 = static_cast<int>((b0 + j) * kBN);
-        unsigned char* kd = smem + kOffK + st * kTile;
-        mbar_arrive_expect_tx(&bar.full_k[st], kTile);
-        if (kv_hint) {
-          tma_load_3d_hint(kd, &tmap_k, &bar.full_k[st], 0, key0, kvh, kv_policy);
-          tma_load_3d_hint(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh, kv_policy);
-        } else {
-          tma_load_3d(kd, &tmap_k, &bar.full_k[st], 0, key0, kvh);
-          tma_load_3d(kd + kHalf, &tmap_k, &bar.full_k[st], 64, key0, kvh);
-        }
+        load_kv(&bar.full_k[st], &tmap_k, smem + kOffK + st * kTile, static_cast<int>((b0 + j) * kBN));
         issued = j + 1;
       }
       if (!q_issued) issue_q();
@@ -280,22 +400,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int j = max(0, issued - 2); j < issued; ++j) mbar_wait_drain(&bar.full_k[j & 1], (j >> 1) & 1);
       }
     } else if (lane == 1) {
-      int issued = 0;
-      for (int j = 0; j < nb; ++j) {
+      int issued = pre;
+      for (int j = pre; j < nb; ++j) {
         if (j == pre) pdl_wait();
         const int st = j & 1;
         // stage st is free once PV(j-2) has consumed it
         if (!mbar_wait(&bar.empty_v[st], ((j >> 1) & 1) ^ 1, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT)) break;
-        const int key0 = static_cast<int>((b0 + j) * kBN);
-        unsigned char* vd = smem + kOffV + st * kTile;
-        mbar_arrive_expect_tx(&bar.full_v[st], kTile);
-        if (kv_hint) {
-          tma_load_3d_hint(vd, &tmap_v, &bar.full_v[st], 0, key0, kvh, kv_policy);
-          tma_load_3d_hint(vd + kHalf, &tmap_v, &bar.full_v[st], 64, key0, kvh, kv_policy);
-        } else {
-          tma_load_3d(vd, &tmap_v, &bar.full_v[st], 0, key0, kvh);
-          tma_load_3d(vd + kHalf, &tmap_v, &bar.full_v[st], 64, key0, kvh);
-        }
+        load_kv(&bar.full_v[st], &tmap_v, smem + kOffV + st * kTile, static_cast<int>((b0 + j) * kBN));
         issued = j + 1;
       }
       if (*abort_flag)
@@ -493,7 +604,26 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bar.xchg[half][r] = l;
     asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxThreads) : "memory");
     const float lrow = bar.xchg[0][r] + bar.xchg[1][r];
-    if (ok && warp_live) {
+    if (p.merge > 1) {
+      // park the unnormalised O rows and (m, l) for the in-cluster merge (the
+      // ring is idle: every load was consumed and the last PV product is final)
+      if (ok && warp_live) {
+        tc_fence_after();
+#pragma unroll
+        for (int c2 = 0; c2 < 2; ++c2) {
+          uint32_t o[32];
+          tmem_ld32(tmem + lane_base + 2 * kBN + col0 + c2 * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<uint4*>(smem + stage_off(r, (col0 + c2 * 32) / 4 + q)) =
+                make_uint4(o[q * 4], o[q * 4 + 1], o[q * 4 + 2], o[q * 4 + 3]);
+        }
+      }
+      if (half == 0)
+        reinterpret_cast<float2*>(smem + kOffMl)[r] =
+            (ok && warp_live) ? make_float2(m, lrow) : make_float2(-INFINITY, 0.f);
+    } else if (ok && warp_live) {
       tc_fence_after();
       const int64_t rows_ws = static_cast<int64_t>(p.tiles) * kBM;
       const int h = valid ? kvh * G + (R - node * G) : 0;
@@ -531,6 +661,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     tc_fence_before();
   }
   __syncthreads();
+  if (p.merge > 1) merge_splits(p, smem, split, kvh, row0, rows_total);
   if (warp == kMmaWarp) {
     __syncwarp();
     tc_fence_after();
@@ -818,22 +949,105 @@ static int default_splits(int n, int G, int hkv, int64_t prefix_len, bool tc) {
 
 static bool use_tc(int n, int G, int path) { return path == 1 || (path == 0 && n * G >= 64); }
 
+// Clusters of `c` tcgen05-path CTAs (cluster (c, 1, 1)) that fit on the GPU at
+// once (0 when the query fails, e.g. without a device); cached per size.
+static int clusters_fit(int c) {
+  static std::mutex mu;
+  static int cache[kMaxMerge + 1] = {};
+  static bool done[kMaxMerge + 1] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (c < 2 || c > kMaxMerge) return 0;
+  if (done[c]) return cache[c];
+  int n = 0;
+  if (cudaFuncSetAttribute(tree_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(kAttnSmem)) == cudaSuccess &&
+      (c <= 8 || cudaFuncSetAttribute(tree_attn_tc_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+                     cudaSuccess)) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(c, 1, 1);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = kAttnSmem;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = static_cast<unsigned>(c);
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, tree_attn_tc_kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();
+  cache[c] = n;
+  done[c] = true;
+  return n;
+}
+
+// How a launch runs: the path, the key splits, and whether the splits of a
+// (kv head, tile) are merged inside the kernel by a cluster of `splits` CTAs
+// (tcgen05 path, 2..16 splits, every cluster resident at once) or by the
+// combine kernel through the caller's workspace.
+struct AttnPlan {
+  bool tc;
+  int splits;
+  bool merge;
+};
+
+static AttnPlan plan_attn(int n, int G, int hkv, int64_t prefix_len, int num_splits, int path) {
+  AttnPlan pl{use_tc(n, G, path), num_splits, false};
+  if (!pl.tc) {
+    if (pl.splits <= 0) pl.splits = default_splits(n, G, hkv, prefix_len, false);
+    return pl;
+  }
+  const int pairs = hkv * tiles_for(n, G);
+  const int64_t nblk = (prefix_len + n + kBN - 1) / kBN;
+  if (num_splits > 0) {
+    // a requested split count is merged in the kernel when its clusters fit
+    pl.merge = num_splits >= 2 && num_splits <= kMaxMerge && pairs <= clusters_fit(num_splits);
+    return pl;
+  }
+  pl.splits = default_splits(n, G, hkv, prefix_len, true);
+  if (pl.splits < 2) return pl;
+  // the largest cluster (<= the one-wave split count) whose clusters all fit at once
+  const int want = static_cast<int>(std::min<int64_t>(std::min<int64_t>(kMaxMerge, nblk), 148 / pairs));
+  for (int c = want; c >= 2; --c) {
+    if (pairs <= clusters_fit(c)) {
+      pl.splits = c;
+      pl.merge = true;
+      return pl;
+    }
+  }
+  return pl;
+}
+
 }  // namespace rt
 
 using namespace rt;
 
 extern "C" int rt_tree_attn_default_splits(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len) {
-  if (n <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return 1;
+  if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads) return 1;
   const int G = num_q_heads / num_kv_heads;
-  return default_splits(n, G, num_kv_heads, prefix_len, use_tc(n, G, 0));
+  return plan_attn(n, G, num_kv_heads, prefix_len, 0, 0).splits;
 }
 
+extern "C" int rt_tree_attn_plan(int n, int num_q_heads, int num_kv_heads, int64_t prefix_len, int num_splits,
+                                 int path, int* splits_out, int* merged_out, int* tcgen05_out) {
+  if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || path < 0 || path > 2)
+    return RT_ERR_INVALID_ARGUMENT;
+  const AttnPlan pl = plan_attn(n, num_q_heads / num_kv_heads, num_kv_heads, prefix_len, num_splits, path);
+  if (splits_out) *splits_out = pl.splits;
+  if (merged_out) *merged_out = pl.merge ? 1 : 0;
+  if (tcgen05_out) *tcgen05_out = pl.tc ? 1 : 0;
+  return RT_OK;
+}
+
+// Bytes of workspace a launch of this shape may need, whatever path it takes
+// (a launch whose splits merge in the kernel uses none of it).
 extern "C" size_t rt_tree_attn_workspace_size(int n, int num_q_heads, int num_kv_heads, int head_dim,
                                               int64_t prefix_len, int num_splits) {
-  if (n <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads || head_dim != kHD) return 0;
+  if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || head_dim != kHD) return 0;
   const int G = num_q_heads / num_kv_heads;
-  if (num_splits <= 0) num_splits = default_splits(n, G, num_kv_heads, prefix_len, use_tc(n, G, 0));
-  if (num_splits == 1) return 0;
+  if (num_splits <= 0) num_splits = plan_attn(n, G, num_kv_heads, prefix_len, 0, 0).splits;
+  if (num_splits <= 1) return 0;
   const size_t rows_ws = static_cast<size_t>(tiles_for(n, G)) * kBM;
   const size_t slots = static_cast<size_t>(num_splits) * num_kv_heads * rows_ws;
   return align_up(slots * kHD * 4, 256) + align_up(slots * 8, 256);
@@ -860,10 +1074,11 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
   if (align_bits & 15) return RT_ERR_INVALID_ARGUMENT;
   if (path < 0 || path > 2) return RT_ERR_INVALID_ARGUMENT;
   const int G = num_q_heads / num_kv_heads;
-  const bool tc = use_tc(n, G, path);
+  const AttnPlan plan = plan_attn(n, G, num_kv_heads, prefix_len, num_splits, path);
+  const bool tc = plan.tc;
   if (!tc && n * G > 64) return RT_ERR_UNSUPPORTED;  // warp-level path holds <= 64 rows
   if (kv_capacity > INT32_MAX) return RT_ERR_UNSUPPORTED;
-  if (num_splits <= 0) num_splits = default_splits(n, G, num_kv_heads, prefix_len, tc);
+  num_splits = plan.splits;
   AttnParams p{};
   p.q = static_cast<const char*>(q);
   p.q_tok_stride = q_tok_stride;
@@ -880,6 +1095,7 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
   p.num_kv_heads = num_kv_heads;
   p.tiles = tiles_for(n, G);
   p.num_splits = num_splits;
+  p.merge = plan.merge ? num_splits : 1;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   p.k = static_cast<const char*>(k);
@@ -887,7 +1103,7 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
   p.kv_head_stride = kv_head_stride;
   p.kv_row_stride = kv_row_stride;
   if (l2_ranges_from(prefetch, &p.pf) != RT_OK) return RT_ERR_INVALID_ARGUMENT;
-  if (num_splits > 1) {
+  if (num_splits > 1 && !plan.merge) {
     const size_t need = rt_tree_attn_workspace_size(n, num_q_heads, num_kv_heads, head_dim, prefix_len, num_splits);
     if (workspace == nullptr || workspace_bytes < need) return RT_ERR_WORKSPACE;
     const size_t rows_ws = static_cast<size_t>(p.tiles) * kBM;
@@ -910,8 +1126,10 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
     }
     set_smem_limit(tree_attn_tc_kernel, kAttnSmem);
     const dim3 grid(num_splits, num_kv_heads, p.tiles);
-    rc = record_cuda(launch_ex(tree_attn_tc_kernel, grid, dim3(kAttnThreads), kAttnSmem, s, 1, tk, tv, tq, p, q_tma));
+    rc = record_cuda(launch_ex_cluster(tree_attn_tc_kernel, grid, dim3(kAttnThreads), kAttnSmem, s,
+                                       dim3(plan.merge ? num_splits : 1, 1, 1), tk, tv, tq, p, q_tma));
     if (rc != RT_OK) return rc;
+    if (plan.merge) return RT_OK;
   } else {
     const dim3 grid(num_splits, num_kv_heads);
     int rc = record_cuda(launch_ex(tree_attn_simt_kernel, grid, dim3(128), 0, s, 1, p));
@@ -991,11 +1209,11 @@ extern "C" int rt_tree_attn_noalloc(const void* q, int64_t q_tok_stride, int64_t
                                     float scale, int num_splits, int path, int* status, rt_stream_t stream) {
   if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || head_dim <= 0)
     return RT_ERR_INVALID_ARGUMENT;
-  if (num_splits <= 0) {
-    const int G = num_q_heads / num_kv_heads;
-    num_splits = rt::default_splits(n, G, num_kv_heads, prefix_len, rt::use_tc(n, G, path));
-  }
-  const size_t need = rt_tree_attn_workspace_size(n, num_q_heads, num_kv_heads, head_dim, prefix_len, num_splits);
+  const int G = num_q_heads / num_kv_heads;
+  const rt::AttnPlan plan = rt::plan_attn(n, G, num_kv_heads, prefix_len, num_splits, path);
+  num_splits = plan.splits;
+  const size_t need =
+      plan.merge ? 0 : rt_tree_attn_workspace_size(n, num_q_heads, num_kv_heads, head_dim, prefix_len, num_splits);
   if (need > rt::kNoAllocScratchBytes) return RT_ERR_WORKSPACE;  // beyond the fixed scratch: use rt_tree_attn
   void* ws = nullptr;
   if (need > 0) {

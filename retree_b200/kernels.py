@@ -240,8 +240,8 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
     words = mask_bits.stride(0)
     scale = d ** -0.5 if scale is None else float(scale)
     cap = k.shape[1] if kv_capacity is None else int(kv_capacity)
-    splits = num_splits if num_splits > 0 else lib.rt_tree_attn_default_splits(n, hq, hkv, int(prefix_len))
-    ws_bytes = lib.rt_tree_attn_workspace_size(n, hq, hkv, d, int(prefix_len), splits)
+    splits, merged = attn_plan(n, hq, hkv, int(prefix_len), num_splits, path)
+    ws_bytes = 0 if merged else lib.rt_tree_attn_workspace_size(n, hq, hkv, d, int(prefix_len), splits)
     ws = _STATE.buffer(q.device, "attn_ws", ws_bytes) if ws_bytes else None
     pf = _l2_ranges(l2_prefetch) if l2_prefetch else None
     rc = lib.rt_tree_attn_ex(q.data_ptr(), q.stride(0) * es, q.stride(1) * es, k.data_ptr(), v.data_ptr(),
@@ -251,7 +251,7 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
                              None if pf is None else ctypes.addressof(pf), _STATE.status(q.device).data_ptr(),
                              _stream(q.device))
     _lib.check(rc, "rt_tree_attn")
-    _count(2 if splits > 1 else 1)
+    _count(2 if ws_bytes else 1)  # the combine launch runs only when the partials go through the workspace
     return out
 
 
@@ -278,6 +278,15 @@ def l2_prefetch(ranges, ctas: int = 16, device=None) -> None:
     dev = ranges[0][0].device if device is None else device
     _lib.check(_lib.load().rt_l2_prefetch(ctypes.addressof(pf), int(ctas), _stream(dev)), "rt_l2_prefetch")
     _count()
+
+
+def attn_plan(n: int, num_q_heads: int, num_kv_heads: int, prefix_len: int, num_splits: int = 0,
+              path: int = 0) -> tuple[int, bool]:
+    """(key splits, merged in the kernel) of an rt_tree_attn launch of this shape (rt_tree_attn_plan)."""
+    sp, mg = ctypes.c_int(0), ctypes.c_int(0)
+    _lib.check(_lib.load().rt_tree_attn_plan(n, num_q_heads, num_kv_heads, int(prefix_len), int(num_splits), int(path),
+                                             ctypes.byref(sp), ctypes.byref(mg), None), "rt_tree_attn_plan")
+    return sp.value, bool(mg.value)
 
 
 def default_splits(n: int, num_q_heads: int, num_kv_heads: int, prefix_len: int) -> int:

@@ -53,12 +53,12 @@ class RecoveryTable:
 
     @classmethod
     def from_memory(cls, memory: RecoveryMemory, capacity: int | None = None, extra_pairs: int = 1 << 16):
-        pairs = set(memory.prior_counts()) | set(memory.online_counts())
-        t = cls(capacity or cls.capacity_for(len(pairs) + extra_pairs))
-        for (d, g), c in memory.prior_counts().items():
-            t.prior[t.insert(d, g)] += c
-        for (d, g), c in memory.online_counts().items():
-            t.online[t.insert(d, g)] += c
+        """The table of ``memory``'s pair rows (both counts of a pair in one slot)."""
+        t = cls(capacity or cls.capacity_for(memory.total_pairs() + extra_pairs))
+        for d, g, prior, online in memory.rows():
+            s = t.insert(d, g)
+            t.prior[s] += prior
+            t.online[s] += online
         return t
 
     def _slot(self, key: np.uint64, insert: bool) -> int:

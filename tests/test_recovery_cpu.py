@@ -116,3 +116,40 @@ def test_files_match_the_reference_writer_byte_for_byte(golden_dir):
     assert loaded.prior_counts() == mem.prior_counts() and loaded.online_counts() == mem.online_counts()
     flat = RecoveryMemory.from_file(f"{golden_dir}/recovery_prior.json")
     assert flat.prior_counts() == mem.prior_counts() and flat.online_counts() == {}
+
+
+def test_pair_table_orders_and_totals():
+    """Iteration and tie order follow when each pair became present in each table; totals count
+    positive entries only; clearing the online counts leaves the prior untouched."""
+    m = RecoveryMemory(freq_threshold=2)
+    m.record_online(5, 6)          # online-only pair, first of all
+    m.record_prior(1, 2, count=2)
+    m.record_prior(3, 4, count=2)
+    m.record_online(1, 2)
+    m.record_prior(5, 6, count=1)  # now in both tables
+    assert list(m.prior_counts()) == [(1, 2), (3, 4), (5, 6)]
+    assert list(m.online_counts()) == [(5, 6), (1, 2)]
+    # combined counts (1,2)=3, (3,4)=2, (5,6)=2: ties keep prior order
+    assert m.top_k_pairs(3) == [((1, 2), 3), ((3, 4), 2), ((5, 6), 2)]
+    assert (m.prior_total_pairs(), m.online_total_pairs(), m.total_pairs()) == (3, 2, 3)
+    assert (m.prior_total_events(), m.online_total_events(), m.total_rejections()) == (5, 2, 7)
+    m.get_frequency(9, 9)          # a lookup creates nothing
+    assert m.total_pairs() == 3
+    m.clear_online()
+    assert m.online_counts() == {} and m.total_pairs() == 3 and m.get_frequency(1, 2) == 2
+    m.record_online(3, 4)
+    assert list(m.online_counts()) == [(3, 4)]
+    assert [r for r in m.rows()] == [(5, 6, 1, 0), (1, 2, 2, 0), (3, 4, 2, 1)]
+
+
+def test_divergence_recording_stops_at_top_k_without_reading_further():
+    m = RecoveryMemory()
+    seen = []
+
+    def ranked():
+        for t in (7, 20, 8, 9, 10):
+            seen.append(t)
+            yield t
+
+    assert m.record_online_divergences(ranked(), target_token=20, top_k=2, stop_token_ids=None) == 2
+    assert seen == [7, 20, 8] and m.online_counts() == {(7, 20): 1, (8, 20): 1}

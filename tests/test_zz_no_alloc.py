@@ -36,14 +36,14 @@ def _case(seed, n, prefix, dev):
     return q, kv[0], kv[1], bits
 
 
-def _noalloc(q, k, v, bits, prefix, status, stream):
+def _noalloc(q, k, v, bits, prefix, splits, status, stream):
     lib = _lib.load()
     n = q.shape[0]
     out = torch.full_like(q, float("nan"))
     rc = lib.rt_tree_attn_noalloc(q.data_ptr(), q.stride(0) * 2, q.stride(1) * 2, k.data_ptr(), v.data_ptr(),
                                   k.stride(0) * 2, k.stride(1) * 2, k.shape[1], out.data_ptr(), out.stride(0) * 2,
                                   out.stride(1) * 2, bits.data_ptr(), bits.shape[1], n, prefix, None, 32, 8, 128,
-                                  ctypes.c_float(128 ** -0.5), 0, 0, status.data_ptr(), stream)
+                                  ctypes.c_float(128 ** -0.5), splits, 0, status.data_ptr(), stream)
     assert rc == _lib.RT_OK, _lib.status_string(rc)
     return out
 
@@ -57,12 +57,16 @@ def test_noalloc_matches_workspace_entry_point_twice():
     assert lib.rt_tree_attn_noalloc_max_bytes() == 16 << 20
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    # two calls in a row: a budget-16 tree over 4096 keys (17 key splits), then a
-    # budget-64 tree over 2048 keys -- the second reuses the array the first left behind
-    for seed, n, prefix in ((1, 17, 4096), (2, 65, 2048)):
+    # two calls in a row, each with more key splits than one cluster merges (so the
+    # partials go through the fixed array): a budget-16 tree over 4096 keys in 20
+    # splits, then a 29-node tree over 2048 keys in 18 -- the second reuses the
+    # array the first left behind
+    for seed, n, prefix, splits in ((1, 17, 4096, 20), (2, 29, 2048, 18)):
         q, k, v, bits = _case(seed, n, prefix, dev)
-        got = _noalloc(q, k, v, bits, prefix, status, stream)
-        want = kernels.tree_attention(q, k, v, bits, prefix)
+        assert 0 < lib.rt_tree_attn_workspace_size(n, 32, 8, 128, prefix, splits) <= \
+            lib.rt_tree_attn_noalloc_max_bytes()
+        got = _noalloc(q, k, v, bits, prefix, splits, status, stream)
+        want = kernels.tree_attention(q, k, v, bits, prefix, num_splits=splits)
         torch.cuda.synchronize()
         assert int(status.item()) == 0
         err = (got.float() - want.float()).abs()
