@@ -238,12 +238,6 @@ __device__ __forceinline__ void merge_splits(const AttnParams& p, unsigned char*
   cluster_sync_all();
 }
 
-__device__ __forceinline__ uint32_t ex2_f16x2(float lo, float hi) {
-  uint32_t h, e;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(h) : "f"(hi), "f"(lo));
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(e) : "r"(h));
-  return e;
-}
 
 __global__ void __launch_bounds__(kAttnThreads, 1)
     tree_attn_tc_kernel(const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -581,12 +575,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           uint32_t pk[4];
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
-            const float x0 = fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t]), sl2, -mu);
-            const float x1 = fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t + 1]), sl2, -mu);
-            const uint32_t e = ex2_f16x2(x0, x1);
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&e));
-            ls[t] += f.x + f.y;
-            pk[t] = pack_bf16x2(f.x, f.y);
+            const float p0 = ex2(fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t]), sl2, -mu));
+            const float p1 = ex2(fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t + 1]), sl2, -mu));
+            ls[t] += p0 + p1;
+            pk[t] = pack_bf16x2(p0, p1);
           }
           const int ch = c2 * 4 + q;  // 16-byte chunk within the 128-byte row
           const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
@@ -1005,16 +997,21 @@ static AttnPlan plan_attn(int n, int G, int hkv, int64_t prefix_len, int num_spl
     pl.merge = num_splits >= 2 && num_splits <= kMaxMerge && pairs <= clusters_fit(num_splits);
     return pl;
   }
-  pl.splits = default_splits(n, G, hkv, prefix_len, true);
+  pl.splits = default_splits(n, G, hkv, prefix_len, true);  // one wave of CTAs
   if (pl.splits < 2) return pl;
   // the largest cluster (<= the one-wave split count) whose clusters all fit at once
-  const int want = static_cast<int>(std::min<int64_t>(std::min<int64_t>(kMaxMerge, nblk), 148 / pairs));
-  for (int c = want; c >= 2; --c) {
-    if (pairs <= clusters_fit(c)) {
-      pl.splits = c;
-      pl.merge = true;
-      return pl;
-    }
+  const int want = static_cast<int>(std::min<int64_t>(std::min<int64_t>(kMaxMerge, nblk), pl.splits));
+  int c = want;
+  while (c >= 2 && pairs > clusters_fit(c)) --c;
+  if (c < 2) return pl;
+  // Merged in the kernel when the cluster takes every split of the wave, or
+  // leaves each CTA at most three key blocks (a latency-bound launch, where the
+  // combine launch costs more than the CTAs it would add; measured on B200:
+  // 17 blocks merge faster in a 10-CTA cluster than in 17 workspace splits,
+  // 33 blocks run equally, 257 blocks twice as fast in workspace splits).
+  if (c == pl.splits || nblk <= 3 * c) {
+    pl.splits = c;
+    pl.merge = true;
   }
   return pl;
 }
