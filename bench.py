@@ -119,7 +119,10 @@ def measured_peaks():
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one tree-attention launch, from an ncu capture
 # of the current kernel at the workload's live shape: workload -> (bytes, prefix_len, tree_nodes, how taken).
 # Scaled to the live prefix by the K/V bytes per key when the bench's prefix differs.
-ATTN_TRAFFIC = {}
+ATTN_TRAFFIC = {
+    "qwen3-4b-b16": (8785920, 2075, 17, "ncu dram__bytes_read.sum + dram__bytes_write.sum of one tree_attn_tc_kernel "
+                     "launch, cold L2 (bench_kernels.py single --budget 16 --prefix 2075)"),
+}
 
 
 def attn_traffic(workload: str, prefix_len: int, n_tree: int, hkv: int):

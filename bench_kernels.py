@@ -1,9 +1,9 @@
 """Kernel-level measurements of the verification path (one JSON line per case).
 
-    python -m retree_b200.bench_kernels sweep  [--prefix 4096] [--budgets 16,32,64,128,256] [--layers 36]
-    python -m retree_b200.bench_kernels single --budget 16 --prefix 2048 [--reps 3]
-    python -m retree_b200.bench_kernels parts
-    python -m retree_b200.bench_kernels linear [--m 17,65,257] [--shapes qkv,o,gate_up,down,lm_head]
+    python bench_kernels.py sweep  [--prefix 4096] [--budgets 16,32,64,128,256] [--layers 36]
+    python bench_kernels.py single --budget 16 --prefix 2048 [--reps 3]
+    python bench_kernels.py parts
+    python bench_kernels.py linear [--m 17,65,257] [--shapes qkv,o,gate_up,down,lm_head]
 
 ``sweep`` is the tree-verify attention budget sweep (Qwen3-4B head geometry:
 32 query / 8 KV heads, head_dim 128, bf16): random trees from seeded parent
@@ -23,13 +23,15 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import sys
 
 import numpy as np
 import torch
 
-from . import kernels, synthetic
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+from retree_b200 import kernels, synthetic  # noqa: E402
 HQ, HKV, HD = 32, 8, 128
 
 
@@ -106,7 +108,7 @@ def attention_case(n: int, L: int, layers: int, dev, seed: int = 0, splits: int 
 
 
 def parts(dev) -> list[dict]:
-    from .ddtree import NgramParams
+    from retree_b200.ddtree import NgramParams
     out = []
     logits = torch.from_numpy(synthetic.draft_logits(0, 16, 151936)[-15:]).to(dev).to(torch.bfloat16)
     ctx = torch.from_numpy(synthetic.context_ids(0, 2049, 151936)).to(dev)
@@ -180,7 +182,7 @@ def draft_case(dev, hidden: int = 4096, layers: int = 5, ctx: int = 5, prefix: i
     """
     from torch import nn
 
-    from .draft import FusedDraft, random_draft
+    from retree_b200.draft import FusedDraft, random_draft
 
     ids = [1, 9, 17, 25, 33][:layers]
     draft = random_draft(hidden, layers, 32, 8, 3 * hidden, block, ids, dev)

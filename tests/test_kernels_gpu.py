@@ -228,3 +228,31 @@ def test_mask_from_dense_matches_compile(dtype):
     dense = torch.from_numpy(mask).to(dtype).to(dev)
     bits = kernels.mask_from_dense(dense, 10, len(parents))
     assert np.array_equal(bits.cpu().numpy().view(np.uint32), ot.pack_bits(ot.visibility(parents)))
+
+
+def test_kv_compact_depth_12_path_after_a_32k_prefix():
+    """The long-context workload's commit: a seeded depth-12 accepted path (root + 12 nodes) of a budget-256
+    tree, compacted after a 32768-token prefix in every layer's K and V; the prefix rows stay as they were."""
+    dev = cuda()
+    past, n, layers, heads = 32768, 257, 4, 8
+    # a tree whose seeded chain of 12 nodes (at random increasing indices) hangs off the root; every other
+    # node's parent is an earlier node
+    rng = np.random.default_rng(12)
+    chain = sorted(rng.choice(np.arange(1, n), size=12, replace=False).tolist())
+    parents = [-1] + [int(rng.integers(0, i)) for i in range(1, n)]
+    prev = 0
+    for c in chain:
+        parents[c], prev = prev, c
+    keep = [0] + chain
+    depth = [0] * n
+    for i in range(1, n):
+        depth[i] = depth[parents[i]] + 1
+    assert depth[chain[-1]] == 12
+    g = torch.Generator(device=dev).manual_seed(5)
+    slab = torch.randn((2 * layers, heads, past + n + 8, 128), device=dev, generator=g).to(torch.bfloat16)
+    ref = slab.clone()
+    kernels.kv_compact(slab[:, :, : past + n, :], past, torch.tensor(keep, device=dev))
+    kernels.check_device_status(dev)
+    assert torch.equal(slab[:, :, :past], ref[:, :, :past])
+    assert torch.equal(slab[:, :, past: past + len(keep)], ref[:, :, [past + i for i in keep]])
+    assert torch.equal(slab[:, :, past + n:], ref[:, :, past + n:])

@@ -96,3 +96,37 @@ def test_tcgen05_device_prefix_length_and_group_sizes():
                                      prefix_len_dev=plen, path=1 if n * (hq // hkv) >= 64 else 0)
         kernels.check_device_status(dev)
         _check(out, q, k, v, prefix, vis)
+
+
+def _gpu_reference(q, k, v, prefix, vis, scale=128 ** -0.5):
+    """fp32 masked GQA attention on the device (the same op as oracle.attention), one kv head at a time."""
+    n, hq, d = q.shape
+    hkv = k.shape[0]
+    G = hq // hkv
+    s = prefix + n
+    mask = torch.zeros((n, s), dtype=torch.float32, device=q.device)
+    mask[:, prefix:] = torch.where(torch.from_numpy(vis).to(q.device), 0.0, torch.finfo(torch.float32).min)
+    out = torch.empty((n, hq, d), dtype=torch.float32, device=q.device)
+    for h in range(hkv):
+        qh = q[:, h * G:(h + 1) * G].float().transpose(0, 1)            # [G, n, D]
+        sc = torch.matmul(qh, k[h, :s].float().t()) * scale + mask       # [G, n, S]
+        out[:, h * G:(h + 1) * G] = torch.matmul(torch.softmax(sc, dim=-1), v[h, :s].float()).transpose(0, 1)
+    return out
+
+
+@pytest.mark.parametrize("hq,hkv", [(32, 8), (16, 4), (8, 2), (4, 1)])
+def test_long_context_budget_256_at_split_head_counts(hq, hkv):
+    """The long-context workload: prefix 32768, budget 256 (257 tree rows), with the query / kv heads one
+    rank holds when Qwen3-8B's 32 / 8 heads are split by kv head over 1, 2, 4 or 8 GPUs."""
+    dev = cuda()
+    n, prefix = 257, 32768
+    parents, vis = random_tree(5000 + hq, n - 1)
+    g = torch.Generator(device=dev).manual_seed(hq * 31 + hkv)
+    q = torch.randn((n, hq, 128), device=dev, generator=g).to(torch.bfloat16)
+    kv = torch.randn((2, hkv, prefix + n + 64, 128), device=dev, generator=g).to(torch.bfloat16)
+    out = kernels.tree_attention(q, kv[0], kv[1], bits_tensor(vis, dev), prefix)
+    kernels.check_device_status(dev)
+    ref = _gpu_reference(q, kv[0], kv[1], prefix, vis)
+    err = (out.float() - ref).abs()
+    assert float(err.max()) <= MAX_ABS, float(err.max())
+    assert float(err.mean()) <= MEAN_ABS, float(err.mean())
