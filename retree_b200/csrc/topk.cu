@@ -11,6 +11,10 @@
 //      concatenated survivors (still in index order, so ties keep resolving to
 //      the smallest index), bitonic-sorts them by (value desc, index asc),
 //      merges the logsumexp partials and writes logp = fp32(top - log_z).
+#include <cuda_fp16.h>
+
+#include <type_traits>
+
 #include "common.cuh"
 #include "host_util.h"
 
@@ -31,6 +35,12 @@ __device__ __forceinline__ float key_value(uint32_t k) {
   if (k == 0xFFFFFFFFu) return __uint_as_float(0x7FC00000u);
   const uint32_t b = (k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k;
   return __uint_as_float(b);
+}
+
+// 8-bit digit passes that decide a key widened from T (its significant leading bits).
+template <typename T>
+__host__ __device__ constexpr int key_passes() {
+  return sizeof(T) == 4 ? 4 : (std::is_same<T, __half>::value ? 3 : 2);
 }
 
 template <typename T>
@@ -80,16 +90,20 @@ struct SelectShared {
 
 // Select the `k` largest of keys[0..len) (ties -> smaller position first) and
 // write them, in position order, to out_key/out_idx (idx = idx_base + position,
-// or idx_in[position] when idx_in is non-null).
+// or idx_in[position] when idx_in is non-null).  `passes` 8-bit digits decide
+// (4 for fp32 logits; keys widened from bf16 / fp16 carry only their top 16 /
+// 24 bits, the rest being all zeros for positive and all ones for negative
+// values, so 2 / 3 digit passes find the k-th key).
 __device__ void block_select(const uint32_t* keys, const int* idx_in, int idx_base, int len, int k,
-                             uint32_t* out_key, int* out_idx, SelectShared& sh) {
+                             uint32_t* out_key, int* out_idx, SelectShared& sh, int passes) {
   const int tid = threadIdx.x;
   if (tid == 0) {
     sh.prefix = 0;
     sh.need = k;
   }
   uint32_t himask = 0;
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  const int last_shift = 32 - 8 * passes;
+  for (int shift = 24; shift >= last_shift; shift -= 8) {
     sh.hist[tid] = 0;  // kTopkThreads == 256 bins
     __syncthreads();
     const uint32_t prefix = sh.prefix;
@@ -139,7 +153,9 @@ __device__ void block_select(const uint32_t* keys, const int* idx_in, int idx_ba
     himask |= 0xFFu << shift;
     __syncthreads();
   }
-  const uint32_t T = sh.prefix;
+  // the k-th key: the selected digits, and below them the fill of its sign
+  const uint32_t low = last_shift > 0 ? (1u << last_shift) - 1u : 0u;
+  const uint32_t T = sh.prefix | ((sh.prefix & 0x80000000u) ? 0u : low);
   const int eq_take = sh.need;
   // Stable compaction over contiguous per-thread ranges (position order).
   const int per = (len + kTopkThreads - 1) / kTopkThreads;
@@ -204,10 +220,25 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(const T* __res
   m = red_f[0];
 #pragma unroll
   for (int w = 1; w < kTopkThreads / 32; ++w) m = fmaxf(m, red_f[w]);
+  // sum of exp(x - m): each term in fp32 (expf, within 2 ulp; x - m is exact
+  // whenever x is within a factor of two of m, which covers every term that
+  // carries weight), summed in binary64, so the rounded log_z stays within an
+  // ulp of the all-binary64 one
   double s = 0.0;
   if (m > -INFINITY && m < INFINITY) {
-    const double md = static_cast<double>(m);
-    for (int i = tid; i < len; i += kTopkThreads) s += exp(static_cast<double>(key_value(keys[i])) - md);
+    float f[4] = {0.f, 0.f, 0.f, 0.f};
+    double d = 0.0;
+    int c = 0;
+    for (int i = tid; i < len; i += kTopkThreads, ++c) {
+      f[c & 3] = expf(key_value(keys[i]) - m);
+      if ((c & 3) == 3) {
+        d += static_cast<double>(f[0]) + static_cast<double>(f[1]) + static_cast<double>(f[2]) +
+             static_cast<double>(f[3]);
+        f[0] = f[1] = f[2] = f[3] = 0.f;
+      }
+    }
+    s = d + (static_cast<double>(f[0]) + static_cast<double>(f[1]) + static_cast<double>(f[2]) +
+             static_cast<double>(f[3]));
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xFFFFFFFFu, s, o);
@@ -220,10 +251,11 @@ __global__ void __launch_bounds__(kTopkThreads) topk_chunk_kernel(const T* __res
   }
   const int kk = min(k, len);
   const int64_t base = (static_cast<int64_t>(row) * n_chunks + chunk) * k;
-  block_select(keys, nullptr, c0, len, kk, cand_key + base, cand_idx + base, sh);
+  block_select(keys, nullptr, c0, len, kk, cand_key + base, cand_idx + base, sh, key_passes<T>());
 }
 
 __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(int vocab, int k, int chunk_len, int n_chunks,
+                                                                  int passes,
                                                                   const uint32_t* __restrict__ cand_key,
                                                                   const int* __restrict__ cand_idx,
                                                                   const double2* __restrict__ lse_part,
@@ -278,7 +310,7 @@ __global__ void __launch_bounds__(kTopkThreads) topk_merge_kernel(int vocab, int
   // select the row's top k (in index order), staging them in the sort buffer
   uint32_t* sel_key = reinterpret_cast<uint32_t*>(srt);  // reuse: packed below
   int* sel_idx = reinterpret_cast<int*>(sel_key + sort_len);
-  block_select(keys, idx, 0, total, k, sel_key, sel_idx, sh);
+  block_select(keys, idx, 0, total, k, sel_key, sel_idx, sh, passes);
   // pack (key desc, index asc) into 64-bit keys, pad to the power-of-two length
   // (sort_len <= 1024: at most 4 per thread; threads past a short length idle)
   unsigned long long packed[4];
@@ -399,7 +431,8 @@ extern "C" int rt_draft_topk(const void* logits, int dtype, int64_t ld, int rows
   int rc = check_launch();
   if (rc != RT_OK) return rc;
   set_smem_limit(topk_merge_kernel, p.smem2);
-  topk_merge_kernel<<<rows, kTopkThreads, p.smem2, s>>>(vocab, k, p.chunk_len, p.n_chunks, ck, ci, lse, top_logp,
-                                                        top_ids, log_z, p.sort_len);
+  const int passes = dtype == 0 ? key_passes<float>() : dtype == 1 ? key_passes<__nv_bfloat16>() : key_passes<__half>();
+  topk_merge_kernel<<<rows, kTopkThreads, p.smem2, s>>>(vocab, k, p.chunk_len, p.n_chunks, passes, ck, ci, lse,
+                                                        top_logp, top_ids, log_z, p.sort_len);
   return check_launch();
 }

@@ -88,14 +88,16 @@ def retree_generate(model, target, input_ids, mask_token_id, max_new_tokens, blo
                     temperature: float = 0.0, tree_budget: int | None = None,
                     recovery_memory: RecoveryMemory | None = None, gate_threshold: float = 0.01,
                     recovery_online_update: bool = True, recovery_record_top_k: int = 8,
-                    recovery_rescue_top_k: int = 8, draft_fn=None, device_recovery: bool = False,
+                    recovery_rescue_top_k: int = 8, draft_fn=None, device_recovery: bool = True,
                     fused: bool | None = None, fused_draft: bool = False):
     """ReTree decode loop (retree.py:193-444); ``total_rescued`` counts sibling rescues.
 
-    ``device_recovery`` runs the recovery walk on the GPU (rt_recovery_walk)
-    over a device copy of ``recovery_memory``; its online counts are applied to
-    ``recovery_memory`` when the request ends.  ``fused`` / ``fused_draft`` as
-    in ``ddtree_generate``.
+    ``device_recovery`` (the default) runs the recovery walk on the GPU
+    (rt_recovery_walk) over a device copy of ``recovery_memory``, so a round
+    is one graph replay with no per-candidate host round trip; its online
+    counts are applied to ``recovery_memory`` when the request ends.  False
+    walks on the host with the reference's control flow.  ``fused`` /
+    ``fused_draft`` as in ``ddtree_generate``.
     """
     from .verify import TreeVerifier
 

@@ -30,8 +30,11 @@ from oracle import dflash as od  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("RETREE_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("RETREE_REFERENCE"),
+                    help="checkout of the reference repository (or set RETREE_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or RETREE_REFERENCE) must name the reference checkout")
     sys.path.insert(0, args.reference)
     from model.dflash import DFlashDraftModel  # type: ignore
     from transformers import DynamicCache

@@ -393,8 +393,11 @@ def gen_bonus(ddtree):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("RETREE_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("RETREE_REFERENCE"),
+                    help="checkout of the reference repository (or set RETREE_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("--reference (or RETREE_REFERENCE) must name the reference checkout")
     ddtree, retree, recovery = _import_reference(args.reference)
     torch.set_num_threads(max(1, os.cpu_count() or 1))
 

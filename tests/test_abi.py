@@ -1,5 +1,6 @@
 """The C-ABI library loads and exports exactly what include/retree_b200.h declares (CPU only)."""
 
+import os
 import re
 from pathlib import Path
 
@@ -214,22 +215,15 @@ def test_launch_switches_without_gpu():
     assert not kernels.linear_weight_warm_enabled()
 
 
-def test_integration_doc_ctypes_stub_matches_the_library():
-    """The ctypes binding the integration guide shows sets argtypes that agree with the header, and its
-    library path is the built one (the stub runs here up to its first device call)."""
-    import ctypes
+def test_integration_ctypes_stub_matches_the_library():
+    """The ctypes binding INTEGRATION.md points to (tests/integration_stub.py) sets argtypes that agree with
+    the header and loads the built library (it runs here up to its first device call)."""
+    from tests import integration_stub as stub
 
-    doc = (HEADER.parents[1] / "INTEGRATION.md").read_text()
-    blocks = re.findall(r"```python\n(.*?)```", doc, flags=re.S)
-    stub = next(b for b in blocks if "ctypes.CDLL" in b)
-    path = re.search(r'ctypes\.CDLL\("([^"]+)"\)', stub).group(1)
-    assert (HEADER.parents[1] / path).resolve() == _lib.LIB_PATH.resolve()
-    ns: dict = {}
-    exec(compile(stub.replace(path, str(_lib.LIB_PATH)), "INTEGRATION.md", "exec"), ns)
-    lib = ns["lib"]
+    assert os.path.realpath(stub.LIB) == os.path.realpath(str(_lib.LIB_PATH))
     for name in ("rt_kv_compact", "rt_status_string"):
         res, argtypes = _lib.SIGNATURES[name]
-        assert list(getattr(lib, name).argtypes) == list(argtypes), name
-        assert getattr(lib, name).restype is res, name
-    assert lib.rt_status_string(_lib.RT_ERR_INVALID_ARGUMENT).decode() == "invalid argument"
-    assert callable(ns["compact_tail_inplace"])
+        assert list(getattr(stub.lib, name).argtypes) == list(argtypes), name
+        assert getattr(stub.lib, name).restype is res, name
+    assert stub.lib.rt_status_string(_lib.RT_ERR_INVALID_ARGUMENT).decode() == "invalid argument"
+    assert callable(stub.compact_tail_inplace)
