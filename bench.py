@@ -79,14 +79,6 @@ def parse():
                     help="projections of the fused verify forward")
     ap.add_argument("--hf-forward", action="store_true",
                     help="run the verify forward through the transformers modules instead of the fused stages")
-    ap.add_argument("--attn-l2-prefetch", type=float, default=0.0, metavar="MB",
-                    help="MB of the following projections' weights each attention launch warms in L2")
-    ap.add_argument("--l2-stream", action="store_true",
-                    help="warm the next projection's weights in L2 from a side stream next to each launch")
-    ap.add_argument("--linear-warm", action="store_true",
-                    help="rt_linear launches ask the L2 for each CTA's weight rows at entry (long DRAM runs)")
-    ap.add_argument("--kv-l2-prefetch", action="store_true",
-                    help="the QKV projection (rt_linear) warms the L2 with the layer's K/V prefix for the attention")
     ap.add_argument("--fused-argmax", action="store_true",
                     help="the lm_head projection also returns the posterior (rt_linear_argmax), no argmax pass")
     ap.add_argument("--recovery", action="store_true",
@@ -286,8 +278,6 @@ def run_ours(args, wl, rank, world, local_rank):
     from retree_b200.verify import TreeVerifier
 
     os.environ["DDTREE_TREE_STRATEGY"] = args.strategy
-    if args.linear_warm:
-        kernels.set_linear_weight_warm(True)
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
     cfg = qwen3_config(wl["model"])
@@ -314,10 +304,8 @@ def run_ours(args, wl, rank, world, local_rank):
 
     def fresh():
         v = TreeVerifier(target, tree_budget=wl["budget"], max_length=max_len, draft_horizon=wl["block"] - 1,
-                         fused=not args.hf_forward, gemm=args.gemm,
-                         attn_l2_prefetch=int(args.attn_l2_prefetch * 2**20), l2_stream=args.l2_stream,
-                         exchange=args.exchange, fused_argmax=args.fused_argmax,
-                         kv_l2_prefetch=args.kv_l2_prefetch)
+                         fused=not args.hf_forward, gemm=args.gemm, exchange=args.exchange,
+                         fused_argmax=args.fused_argmax)
         if wl.get("split"):
             v.prefill_random(plen, seed=req)
         else:
@@ -550,8 +538,6 @@ def result_line(args, wl, *, world, reqs, steps, warm, dev_s, e2e_s, wall, promp
                    "budget": wl["budget"], "draft_block": wl["block"], "strategy": args.strategy,
                    "verify_forward": "transformers modules" if args.hf_forward else f"fused stages ({args.gemm})",
                    "projections": projections,
-                   "attn_l2_prefetch_mb": args.attn_l2_prefetch, "l2_stream_warm_up": args.l2_stream,
-                   "kv_prefix_l2_warm_up": args.kv_l2_prefetch, "linear_weight_warm_up": args.linear_warm,
                    "walk": "target-gated sibling recovery (device)" if args.recovery else "exact",
                    "posterior": "argmax fused into the lm_head projection" if args.fused_argmax else "torch.argmax",
                    "parallelism": (f"kv-head split over {world} GPUs (attention-output all-gather per layer, "

@@ -62,15 +62,6 @@ const char* rt_status_string(int code);
 void rt_set_pdl(int enabled);
 int rt_pdl_enabled(void);
 
-/* rt_linear launches (all modes) with the weight-row L2 warm-up: at entry the
- * producer warp's idle lanes ask the L2 (cp.async.bulk.prefetch.L2) for each
- * of the CTA's 128 weight rows over its whole K range, one contiguous request
- * per row, so the ring's 128-byte-wide TMA boxes hit L2 and the DRAM sees long
- * runs.  Off by default (RETREE_B200_LINEAR_WARM=1 turns it on); no result
- * depends on it.  No counterpart in the reference. */
-void rt_set_linear_weight_warm(int enabled);
-int rt_linear_weight_warm_enabled(void);
-
 /* ------------------------------------------------------------------------
  * KV-cache compaction after a commit.
  * Replaces compact_tail_inplace / _compact_appended_window
@@ -151,38 +142,6 @@ int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, con
                  int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads, int num_kv_heads,
                  int head_dim, float scale, int num_splits, int path, void* workspace, size_t workspace_bytes,
                  int* status, rt_stream_t stream);
-
-/* ------------------------------------------------------------------------
- * L2 warm-up.
- * No counterpart in the reference.  At tree sizes the verify forward's
- * kernels are bound by latency, not by HBM bandwidth, so while one runs the
- * HBM has room to move the weights the next one reads into the 126 MB L2.
- * A warm-up asks the L2 to load up to RT_L2_MAX_RANGES ranges of device
- * memory with cp.async.bulk.prefetch.L2 requests (32 KB each); nothing waits
- * for them and no result depends on them.  A range with ptr NULL or
- * bytes <= 0 is skipped; ptr must be 16-byte aligned and bytes is rounded
- * down to a multiple of 16; count is 0..RT_L2_MAX_RANGES.
- *
- * rt_l2_prefetch: a kernel of `ctas` one-warp CTAs (1..1024) that issues the
- *   requests (launched on a side stream next to a kernel, it warms what the
- *   following kernel reads).
- * rt_tree_attn_ex: rt_tree_attn whose tcgen05-path CTAs also issue requests
- *   for their share of `prefetch` from the producer warp's idle lanes; same
- *   arguments and results as rt_tree_attn otherwise (prefetch may be NULL).
- * ---------------------------------------------------------------------- */
-#define RT_L2_MAX_RANGES 16
-typedef struct rt_l2_ranges {
-  int count;
-  const void* ptr[RT_L2_MAX_RANGES];
-  int64_t bytes[RT_L2_MAX_RANGES];
-} rt_l2_ranges;
-int rt_l2_prefetch(const rt_l2_ranges* ranges, int ctas, rt_stream_t stream);
-int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
-                    int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
-                    int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words, int n,
-                    int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads, int num_kv_heads,
-                    int head_dim, float scale, int num_splits, int path, void* workspace, size_t workspace_bytes,
-                    const rt_l2_ranges* prefetch, int* status, rt_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Attention-output exchange of a KV-head split over NVLink peer memory.
@@ -436,11 +395,6 @@ int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, rt_stream_t
  *   RT_EPI_QKV_ROPE  W = [Wq; Wk; Wv] (n_out = (Hq + 2 Hkv) * 128): what
  *                    rt_qk_norm_rope_append does with the bf16 result, with
  *                    the arguments of *qkv (out / ld_out unused);
- *   RT_EPI_QKV_ROPE_KV_WARM  the same, and while the weights stream the
- *                    launch asks the L2 for the K/V rows [0, prefix) of every
- *                    kv head of *qkv's cache (prefix = offset + *offset_dev),
- *                    which the attention reads next (cp.async.bulk.prefetch.L2,
- *                    nothing waits; Hkv <= 8).
  * When 128-row tiles alone do not cover the GPU, K is split over a cluster
  * of up to 8 CTAs whose partial sums are added in a fixed order over
  * distributed shared memory: no workspace, results independent of timing.
@@ -449,7 +403,6 @@ int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, rt_stream_t
 #define RT_EPI_STORE 0
 #define RT_EPI_SILU_MUL 1
 #define RT_EPI_QKV_ROPE 2
-#define RT_EPI_QKV_ROPE_KV_WARM 3
 
 typedef struct rt_qkv_epilogue {
   int num_q_heads;

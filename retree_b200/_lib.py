@@ -27,18 +27,13 @@ SIGNATURES = {
     "rt_status_string": (ctypes.c_char_p, [_I]),
     "rt_set_pdl": (None, [_I]),
     "rt_pdl_enabled": (_I, []),
-    "rt_set_linear_weight_warm": (None, [_I]),
-    "rt_linear_weight_warm_enabled": (_I, []),
     "rt_kv_compact": (_I, [_P, _P, _I, _I64, _I, _I64, _I64, _I, _I64, _P, _I64, _P, _I, _P, _P, _P]),
     "rt_kv_append": (_I, [_P, _P, _I64, _I64, _P, _P, _I64, _I64, _I, _I, _I, _I64, _I64, _P, _P, _P]),
     "rt_tree_attn_workspace_size": (_SZ, [_I, _I, _I, _I, _I64, _I]),
     "rt_tree_attn": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
                           _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P]),
-    "rt_tree_attn_ex": (_I, [_P, _I64, _I64, _P, _P, _I64, _I64, _I64, _P, _I64, _I64, _P, _I, _I, _I64, _P,
-                             _I, _I, _I, _F, _I, _I, _P, _SZ, _P, _P, _P]),
     "rt_tree_attn_default_splits": (_I, [_I, _I, _I, _I64]),
     "rt_tree_attn_plan": (_I, [_I, _I, _I, _I64, _I, _I, _P, _P, _P]),
-    "rt_l2_prefetch": (_I, [_P, _I, _P]),
     "rt_ipc_alloc": (_I, [_SZ, _P, _P]),
     "rt_ipc_free": (_I, [_P]),
     "rt_ipc_open": (_I, [_P, _P]),
@@ -72,16 +67,6 @@ SIGNATURES = {
 RT_EPI_STORE = 0
 RT_EPI_SILU_MUL = 1
 RT_EPI_QKV_ROPE = 2
-RT_EPI_QKV_ROPE_KV_WARM = 3
-
-
-RT_L2_MAX_RANGES = 16
-
-
-class L2Ranges(ctypes.Structure):
-    """``rt_l2_ranges`` (include/retree_b200.h): device ranges to warm in L2."""
-
-    _fields_ = [("count", ctypes.c_int), ("ptr", _P * RT_L2_MAX_RANGES), ("bytes", ctypes.c_int64 * RT_L2_MAX_RANGES)]
 
 
 class QkvEpilogue(ctypes.Structure):

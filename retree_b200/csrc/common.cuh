@@ -19,51 +19,6 @@
 namespace rt {
 
 // ---------------------------------------------------------------------------
-// L2 warm-up ranges (validated copy of rt_l2_ranges, passed by value)
-// ---------------------------------------------------------------------------
-struct L2Ranges {
-  int count;
-  const char* ptr[RT_L2_MAX_RANGES];
-  int64_t bytes[RT_L2_MAX_RANGES];  // multiples of 16
-};
-
-// Host: validated device-side copy (NULL -> no ranges).
-inline int l2_ranges_from(const rt_l2_ranges* in, L2Ranges* out) {
-  *out = L2Ranges{};
-  if (in == nullptr) return RT_OK;
-  if (in->count < 0 || in->count > RT_L2_MAX_RANGES) return RT_ERR_INVALID_ARGUMENT;
-  for (int i = 0; i < in->count; ++i) {
-    if (in->ptr[i] == nullptr || in->bytes[i] <= 0) continue;
-    if (reinterpret_cast<uintptr_t>(in->ptr[i]) & 15) return RT_ERR_INVALID_ARGUMENT;
-    out->ptr[i] = static_cast<const char*>(in->ptr[i]);
-    out->bytes[i] = in->bytes[i] & ~static_cast<int64_t>(15);
-  }
-  out->count = in->count;
-  return RT_OK;
-}
-
-// Requests for CTA `cta` of `ctas`'s share of one range (16-byte aligned,
-// `bytes` a multiple of 16) -- bytes [cta*per, (cta+1)*per) -- in 32 KB
-// pieces spread over `parts` threads.
-__device__ __forceinline__ void l2_warm_range(const char* ptr, int64_t bytes, int64_t cta, int64_t ctas, int part,
-                                              int parts) {
-  constexpr int64_t kPiece = 32768;
-  if (ptr == nullptr || bytes <= 0) return;
-  const int64_t per = (((bytes + ctas - 1) / ctas) + 15) & ~static_cast<int64_t>(15);
-  const int64_t b0 = cta * per, b1 = bytes < b0 + per ? bytes : b0 + per;
-  for (int64_t o = b0 + static_cast<int64_t>(part) * kPiece; o < b1; o += static_cast<int64_t>(parts) * kPiece) {
-    const int64_t len = kPiece < b1 - o ? kPiece : b1 - o;
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(ptr + o), "r"(static_cast<uint32_t>(len))
-                 : "memory");
-  }
-}
-
-// The same for every range of `r`.
-__device__ __forceinline__ void l2_warm_share(const L2Ranges& r, int64_t cta, int64_t ctas, int part, int parts) {
-  for (int i = 0; i < r.count; ++i) l2_warm_range(r.ptr[i], r.bytes[i], cta, ctas, part, parts);
-}
-
-// ---------------------------------------------------------------------------
 // Device status word (first error wins)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void set_status(int* status, int code) {
@@ -162,23 +117,6 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, ui
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
           smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y)
-      : "memory");
-}
-
-// L2 policy for data read once (a stream that should not push out what an L2
-// warm-up loaded ahead of its readers).
-__device__ __forceinline__ uint64_t l2_policy_evict_first() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
-
-__device__ __forceinline__ void tma_load_3d_hint(void* smem_dst, const void* tmap, uint64_t* bar, int x, int y,
-                                                 int z, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint "
-      "[%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
       : "memory");
 }
 

@@ -44,10 +44,6 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // stream-serialisation attribute (RETREE_B200_PDL=0 turns it off).
 bool pdl_enabled();
 
-// Whether rt_linear's launches warm the L2 with each CTA's weight rows
-// (RETREE_B200_LINEAR_WARM / rt_set_linear_weight_warm; off by default).
-bool linear_weight_warm();
-
 // cudaLaunchKernelEx with programmatic dependent launch (when enabled) and an
 // optional (1, cluster_y, 1) thread-block cluster.  Every kernel launched
 // through here calls pdl_wait() before it reads or writes data that earlier

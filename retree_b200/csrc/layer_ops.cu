@@ -308,22 +308,3 @@ extern "C" int rt_silu_mul(const void* gate_up, void* out, int rows, int inter, 
   return check_launch();
 }
 
-// ---------------------------------------------------------------------------
-// L2 warm-up kernel: one warp per CTA issues its CTA's share of the ranges.
-// ---------------------------------------------------------------------------
-namespace rt {
-namespace {
-__global__ void __launch_bounds__(32) l2_prefetch_kernel(const L2Ranges r) {
-  l2_warm_share(r, blockIdx.x, gridDim.x, threadIdx.x, 32);
-}
-}  // namespace
-}  // namespace rt
-
-extern "C" int rt_l2_prefetch(const rt_l2_ranges* ranges, int ctas, rt_stream_t stream) {
-  if (ranges == nullptr || ctas < 1 || ctas > 1024) return RT_ERR_INVALID_ARGUMENT;
-  rt::L2Ranges r;
-  if (rt::l2_ranges_from(ranges, &r) != RT_OK) return RT_ERR_INVALID_ARGUMENT;
-  if (r.count == 0) return RT_OK;
-  rt::l2_prefetch_kernel<<<ctas, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(r);
-  return rt::check_launch();
-}

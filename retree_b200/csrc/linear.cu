@@ -70,9 +70,6 @@ struct LinearParams {
   int64_t g_epoch_add;
   // rt_linear_argmax: per token the max of argmax_key over the output row (zeroed before the launch)
   unsigned long long* am_keys;
-  // weight-row L2 warm-up at entry (rt_set_linear_weight_warm)
-  int w_warm;
-  const char* w_ptr;
 };
 
 // kMode: kPlain, kGatherX (X gathered from the ranks of a split, rt_linear_gather)
@@ -234,30 +231,6 @@ __global__ void __launch_bounds__(kLinThreads, 2) linear_kernel(const __grid_con
           mbar_wait_drain(&bar.full[it % p.stages], (it / p.stages) & 1);
       }
     } else {
-      if (p.w_warm) {
-        // this CTA's 128 weight rows over its K range, one contiguous request per row
-        const int64_t c0 = static_cast<int64_t>(kb0) * p.bps * kBK;
-        const int64_t c1 = min(static_cast<int64_t>(kb0 + nk) * p.bps * kBK, static_cast<int64_t>(p.k));
-        for (int r = lane - 1; r < 128 && c1 > c0; r += 31) {
-          const int64_t row = dual ? (r < 64 ? tile * 64 + r : p.n_out / 2 + tile * 64 + (r - 64)) : tile * 128 + r;
-          l2_warm_range(p.w_ptr + (row * p.k + c0) * 2, (c1 - c0) * 2, 0, 1, 0, 1);
-        }
-      }
-      if (p.epi == RT_EPI_QKV_ROPE_KV_WARM) {
-        // the attention that follows reads this layer's K/V prefix: ask the L2 for this
-        // CTA's share of it now (the prefix rows are not written during the forward, so
-        // before the dependency wait); ranges K head 0..Hkv-1, then V
-        const rt_qkv_epilogue& e = p.qkv;
-        const int64_t prefix = e.offset + (e.offset_dev != nullptr ? *e.offset_dev : 0);
-        const int64_t bytes = (prefix > 0 && prefix <= e.capacity ? prefix : 0) * e.cache_row_stride;
-        const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) * blockIdx.y;
-        const int64_t ctas = static_cast<int64_t>(gridDim.x) * gridDim.y;
-        for (int r = 0; r < 2 * e.num_kv_heads; ++r) {
-          const char* base = static_cast<const char*>(r < e.num_kv_heads ? e.k_cache : e.v_cache) +
-                             (r % e.num_kv_heads) * e.cache_head_stride;
-          l2_warm_range(base, bytes, cta, ctas, lane - 1, 31);
-        }
-      }
       pdl_wait();
     }
   } else if (warp == 1) {
@@ -507,7 +480,7 @@ int max_active_clusters(int cluster, size_t smem, int tiles) {
 // with the deeper one-CTA-per-SM ring preferred over two CTAs per SM.
 int make_plan(int m, int n_out, int k, int epi, Plan* pl, bool choose) {
   if (m <= 0 || m > kMaxTokens || k < 8 || k % 8 || n_out <= 0 || n_out % 128) return RT_ERR_INVALID_ARGUMENT;
-  if (epi < RT_EPI_STORE || epi > RT_EPI_QKV_ROPE_KV_WARM) return RT_ERR_INVALID_ARGUMENT;
+  if (epi < RT_EPI_STORE || epi > RT_EPI_QKV_ROPE) return RT_ERR_INVALID_ARGUMENT;
   const int m_pad = (m + 15) / 16 * 16;
   pl->chunks = m_pad > 256 ? 2 : 1;
   pl->chunk_rows = pl->chunks == 1 ? m_pad : ((m_pad / 2 + 15) / 16 * 16);
@@ -583,15 +556,12 @@ extern "C" int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* 
   int rc = make_plan(m, n_out, k, epilogue, &pl, true);
   if (rc != RT_OK) return rc;
   if (!x || !w || !al16(x) || !al16(w) || ld_x < k || (ld_x * 2) % 16) return RT_ERR_INVALID_ARGUMENT;
-  if (epilogue == RT_EPI_QKV_ROPE || epilogue == RT_EPI_QKV_ROPE_KV_WARM) {
+  if (epilogue == RT_EPI_QKV_ROPE) {
     if (!qkv || qkv->num_q_heads <= 0 || qkv->num_kv_heads <= 0 ||
         n_out != (qkv->num_q_heads + 2 * qkv->num_kv_heads) * 128 || !qkv->cos_table || !qkv->sin_table ||
         qkv->table_len <= 0 || !qkv->positions || !qkv->q_out || !qkv->k_cache || !qkv->v_cache ||
         qkv->capacity <= 0 || (qkv->q_norm_weight == nullptr) != (qkv->k_norm_weight == nullptr) ||
         qkv->cache_head_stride % 8 || qkv->cache_row_stride % 8 ||
-        (epilogue == RT_EPI_QKV_ROPE_KV_WARM &&
-         (qkv->num_kv_heads > 8 || qkv->cache_row_stride % 16 || qkv->cache_head_stride % 16 ||
-          reinterpret_cast<uintptr_t>(qkv->k_cache) % 16 || reinterpret_cast<uintptr_t>(qkv->v_cache) % 16)) ||
         reinterpret_cast<uintptr_t>(qkv->k_cache) % 8 || reinterpret_cast<uintptr_t>(qkv->v_cache) % 8 ||
         reinterpret_cast<uintptr_t>(qkv->q_out) % 8)
       return RT_ERR_INVALID_ARGUMENT;
@@ -623,8 +593,6 @@ extern "C" int rt_linear(const void* x, int64_t ld_x, int m, int k, const void* 
   p.ld_out = ld_out;
   if (qkv) p.qkv = *qkv;
   p.status = status;
-  p.w_warm = linear_weight_warm() ? 1 : 0;
-  p.w_ptr = static_cast<const char*>(w);
   set_smem_limit(linear_kernel<kPlain>, pl.smem);
   static const XSources<kPlain> no_sources{};
   return record_cuda(launch_ex(linear_kernel<kPlain>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
@@ -675,8 +643,6 @@ extern "C" int rt_linear_gather(const void* const* x_ranks, int world, int cols_
   p.g_flags = flags_local;
   p.g_epoch = epoch_dev;
   p.g_epoch_add = epoch_add;
-  p.w_warm = linear_weight_warm() ? 1 : 0;
-  p.w_ptr = static_cast<const char*>(w);
   set_smem_limit(linear_kernel<kGatherX>, pl.smem);
   return record_cuda(launch_ex(linear_kernel<kGatherX>, dim3(pl.tiles, pl.splits), dim3(kLinThreads), pl.smem,
                                static_cast<cudaStream_t>(stream), pl.splits, tw, xs.map[0], xs, p));
@@ -723,8 +689,6 @@ extern "C" int rt_linear_argmax(const void* x, int64_t ld_x, int m, int k, const
   p.ld_out = ld_out;
   p.status = status;
   p.am_keys = static_cast<unsigned long long*>(keys);
-  p.w_warm = linear_weight_warm() ? 1 : 0;
-  p.w_ptr = static_cast<const char*>(w);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   rc = record_cuda(cudaMemsetAsync(keys, 0, static_cast<size_t>(m) * 8, s));
   if (rc != RT_OK) return rc;

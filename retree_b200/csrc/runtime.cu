@@ -10,20 +10,7 @@ namespace rt {
 thread_local int g_last_cuda_error = 0;
 
 namespace {
-std::atomic<int> g_pdl{-1};          // -1: not decided yet (environment), 0 off, 1 on
-std::atomic<int> g_linear_warm{-1};  // the same for rt_linear's weight-row L2 warm-up
-}
-
-bool linear_weight_warm() {
-  int v = g_linear_warm.load(std::memory_order_relaxed);
-  if (v < 0) {
-    const char* e = std::getenv("RETREE_B200_LINEAR_WARM");
-    v = (e != nullptr && std::strcmp(e, "0") != 0 && e[0] != '\0') ? 1 : 0;
-    int expected = -1;
-    g_linear_warm.compare_exchange_strong(expected, v);
-    v = g_linear_warm.load(std::memory_order_relaxed);
-  }
-  return v != 0;
+std::atomic<int> g_pdl{-1};  // -1: not decided yet (environment), 0 off, 1 on
 }
 
 bool pdl_enabled() {
@@ -42,10 +29,6 @@ bool pdl_enabled() {
 extern "C" void rt_set_pdl(int enabled) { rt::g_pdl.store(enabled ? 1 : 0); }
 
 extern "C" int rt_pdl_enabled(void) { return rt::pdl_enabled() ? 1 : 0; }
-
-extern "C" void rt_set_linear_weight_warm(int enabled) { rt::g_linear_warm.store(enabled ? 1 : 0); }
-
-extern "C" int rt_linear_weight_warm_enabled(void) { return rt::linear_weight_warm() ? 1 : 0; }
 
 extern "C" int rt_abi_version(void) { return 2; }
 

@@ -81,7 +81,6 @@ struct AttnParams {
   const char* k;
   const char* v;
   int64_t kv_head_stride, kv_row_stride;
-  L2Ranges pf;  // L2 warm-up (rt_tree_attn_ex)
 };
 
 struct Barriers {
@@ -286,17 +285,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   // The producer lane sets up the barriers and sends the pure-prefix K/V loads
   // out at once, while the MMA warp allocates TMEM (nothing before the block
   // barrier below waits for another warp).
-  const bool kv_hint = p.pf.count > 0;  // evict-first K/V loads while an L2 warm-up is in flight
-  const uint64_t kv_policy = kv_hint ? l2_policy_evict_first() : 0ull;
   auto load_kv = [&](uint64_t* full, const CUtensorMap* map, unsigned char* dst, int key0) {
     mbar_arrive_expect_tx(full, kTile);
-    if (kv_hint) {
-      tma_load_3d_hint(dst, map, full, 0, key0, kvh, kv_policy);
-      tma_load_3d_hint(dst + kHalf, map, full, 64, key0, kvh, kv_policy);
-    } else {
-      tma_load_3d(dst, map, full, 0, key0, kvh);
-      tma_load_3d(dst + kHalf, map, full, 64, key0, kvh);
-    }
+    tma_load_3d(dst, map, full, 0, key0, kvh);
+    tma_load_3d(dst + kHalf, map, full, 64, key0, kvh);
   };
   if (warp == kProducerWarp && lane == 0) {
     prefetch_tmap(&tmap_k);
@@ -408,11 +400,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       pdl_wait();
     } else {
       pdl_wait();
-      // idle lanes: warm the L2 with what the following kernels read
-      if (p.pf.count > 0) {
-        const int64_t cta = blockIdx.x + static_cast<int64_t>(gridDim.x) * (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
-        l2_warm_share(p.pf, cta, static_cast<int64_t>(gridDim.x) * gridDim.y * gridDim.z, lane - 2, 30);
-      }
     }
   } else if (warp == kMmaWarp) {
     pdl_wait();
@@ -1050,13 +1037,12 @@ extern "C" size_t rt_tree_attn_workspace_size(int n, int num_q_heads, int num_kv
   return align_up(slots * kHD * 4, 256) + align_up(slots * 8, 256);
 }
 
-extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k,
-                               const void* v, int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity,
-                               void* out, int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask,
-                               int mask_words, int n, int64_t prefix_len, const int64_t* prefix_len_dev,
-                               int num_q_heads, int num_kv_heads, int head_dim, float scale, int num_splits, int path,
-                               void* workspace, size_t workspace_bytes, const rt_l2_ranges* prefetch, int* status,
-                               rt_stream_t stream) {
+extern "C" int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
+                            int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
+                            int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words,
+                            int n, int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads,
+                            int num_kv_heads, int head_dim, float scale, int num_splits, int path, void* workspace,
+                            size_t workspace_bytes, int* status, rt_stream_t stream) {
   if (!q || !k || !v || !out || !mask) return RT_ERR_INVALID_ARGUMENT;
   if (n <= 0 || num_kv_heads <= 0 || num_q_heads <= 0 || num_q_heads % num_kv_heads || prefix_len < 0)
     return RT_ERR_INVALID_ARGUMENT;
@@ -1099,7 +1085,6 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
   p.v = static_cast<const char*>(v);
   p.kv_head_stride = kv_head_stride;
   p.kv_row_stride = kv_row_stride;
-  if (l2_ranges_from(prefetch, &p.pf) != RT_OK) return RT_ERR_INVALID_ARGUMENT;
   if (num_splits > 1 && !plan.merge) {
     const size_t need = rt_tree_attn_workspace_size(n, num_q_heads, num_kv_heads, head_dim, prefix_len, num_splits);
     if (workspace == nullptr || workspace_bytes < need) return RT_ERR_WORKSPACE;
@@ -1136,18 +1121,6 @@ extern "C" int rt_tree_attn_ex(const void* q, int64_t q_tok_stride, int64_t q_he
   // two warps per output row on the combine's fast path (up to kFastSplits splits), one otherwise
   const int warps = num_kv_heads * n * G * (num_splits <= kFastSplits ? 2 : 1);
   return record_cuda(launch_ex(attn_combine_kernel, dim3((warps + 3) / 4), dim3(128), 0, s, 1, p));
-}
-
-extern "C" int rt_tree_attn(const void* q, int64_t q_tok_stride, int64_t q_head_stride, const void* k, const void* v,
-                            int64_t kv_head_stride, int64_t kv_row_stride, int64_t kv_capacity, void* out,
-                            int64_t out_tok_stride, int64_t out_head_stride, const uint32_t* mask, int mask_words,
-                            int n, int64_t prefix_len, const int64_t* prefix_len_dev, int num_q_heads,
-                            int num_kv_heads, int head_dim, float scale, int num_splits, int path, void* workspace,
-                            size_t workspace_bytes, int* status, rt_stream_t stream) {
-  return rt_tree_attn_ex(q, q_tok_stride, q_head_stride, k, v, kv_head_stride, kv_row_stride, kv_capacity, out,
-                         out_tok_stride, out_head_stride, mask, mask_words, n, prefix_len, prefix_len_dev,
-                         num_q_heads, num_kv_heads, head_dim, scale, num_splits, path, workspace, workspace_bytes,
-                         nullptr, status, stream);
 }
 
 // ---------------------------------------------------------------------------

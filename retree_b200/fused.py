@@ -38,8 +38,6 @@ like the library GEMM, in their own summation order.
 
 from __future__ import annotations
 
-import os
-
 import torch
 from torch import nn
 
@@ -114,9 +112,7 @@ class _Layer:
 
 class FusedTarget:
     def __init__(self, model, cache, n_max: int, max_positions: int | None = None, gemm: str = "auto",
-                 capture_layers=None, attn_l2_prefetch: int | None = None, l2_stream: bool | None = None,
-                 l2_stream_budget: int = 64 << 20, exchange: str = "nccl", argmax: bool = False,
-                 kv_l2_prefetch: bool | None = None):
+                 capture_layers=None, exchange: str = "nccl", argmax: bool = False):
         if not supports(model):
             raise RuntimeError(f"FusedTarget does not support this model ({model.config.model_type})")
         cfg = model.config
@@ -184,46 +180,6 @@ class FusedTarget:
             if not self.capture_layers or any(i < 0 or i >= len(self.layers) for i in self.capture_layers):
                 raise ValueError(f"capture_layers must name layers in [0, {len(self.layers)})")
             self.hidden_out = torch.empty((n, len(self.capture_layers) * self.hidden), **e)
-        # L2 warm-up from inside each layer's attention launch: up to this many
-        # bytes of the projections that follow it (o_proj, then the head of
-        # gate|up); the attention is latency-bound and leaves the HBM idle
-        if attn_l2_prefetch is None:
-            attn_l2_prefetch = int(float(os.environ.get("RETREE_B200_ATTN_L2PF_MB", "0")) * (1 << 20))
-        self.attn_l2_prefetch = max(0, int(attn_l2_prefetch))
-        for L in self.layers:
-            L.l2pf = None
-            if self.attn_l2_prefetch > 0:
-                o_bytes = L.o_w.numel() * L.o_w.element_size()
-                first = min(o_bytes, self.attn_l2_prefetch)
-                rest = self.attn_l2_prefetch - first
-                L.l2pf = [(L.o_w, first)] + ([(L.gate_up_w, rest)] if rest > 0 else [])
-        # L2 warm-up on a side stream: next to each launch, a small rt_l2_prefetch
-        # kernel asks the L2 for the weights of the projection after it (at most
-        # l2_stream_budget bytes each): o_proj next to the QKV projection, gate|up
-        # next to the attention and o_proj, down next to gate|up, the next
-        # layer's q|k|v next to down
-        if l2_stream is None:
-            l2_stream = os.environ.get("RETREE_B200_L2_STREAM", "0") not in ("", "0")
-        self.l2_stream = bool(l2_stream)
-        self.l2_stream_budget = max(0, int(l2_stream_budget))
-        self._side = None
-        if self.l2_stream:
-            nb = lambda t: t.numel() * t.element_size()  # noqa: E731
-            cap = self.l2_stream_budget
-            for i, L in enumerate(self.layers):
-                gu = nb(L.gate_up_w)
-                head = min(gu, cap)
-                nxt = self.layers[i + 1].qkv_w if i + 1 < len(self.layers) else self.lm_head
-                L.warm = {"qkv": [(L.o_w, min(nb(L.o_w), cap))],
-                          "attn": [(L.gate_up_w, head)],
-                          "o": [(L.gate_up_w[head // nb(L.gate_up_w[0]):], min(gu - head, cap))] if gu > head else [],
-                          "gate_up": [(L.down_w, min(nb(L.down_w), cap))],
-                          "down": [(nxt, min(nb(nxt), cap))]}
-        # the QKV projection (on rt_linear) asks the L2 for the layer's K/V prefix while
-        # its weights stream (RT_EPI_QKV_ROPE_KV_WARM), so the attention reads it from L2
-        if kv_l2_prefetch is None:
-            kv_l2_prefetch = os.environ.get("RETREE_B200_KV_L2PF", "0") not in ("", "0")
-        self.kv_l2_prefetch = bool(kv_l2_prefetch)
         # the lm_head projection also returns each node's argmax (rt_linear_argmax):
         # the temperature-0 posterior without a pass over the logits
         self.argmax = bool(argmax)
@@ -360,8 +316,7 @@ class FusedTarget:
         n = xn.shape[0]
         kc, vc = self.cache.slab[2 * L.index], self.cache.slab[2 * L.index + 1]
         if self.use_rt["qkv"] and L.qkv_b is None and kernels.linear_supported(n, L.qkv_w.shape[0], xn.shape[1], 2):
-            # epilogue 3 also warms the L2 with this layer's K/V prefix for the attention that follows
-            kernels.linear(xn, L.qkv_w, epilogue=3 if self.kv_l2_prefetch and L.hkv <= 8 else 2,
+            kernels.linear(xn, L.qkv_w, epilogue=2,
                            qkv=dict(num_q_heads=L.hq, num_kv_heads=L.hkv, q_norm=L.q_norm, k_norm=L.k_norm,
                                     eps=L.eps_qk, cos=self.cos, sin=self.sin, positions=positions, q_out=self.q[:n],
                                     k_cache=kc, v_cache=vc, offset=offset, offset_dev=offset_dev))
@@ -369,18 +324,6 @@ class FusedTarget:
         self._linear(xn, L.qkv_w, L.qkv_b, self.qkv[:n], kind="qkv")
         kernels.qk_norm_rope_append(self.qkv[:n], L.hq, L.hkv, L.q_norm, L.k_norm, L.eps_qk, self.cos, self.sin,
                                     positions, self.q[:n], kc, vc, offset=offset, offset_dev=offset_dev)
-
-    def _warm(self, L, kind: str) -> None:
-        """Launch the L2 warm-up planned next to ``kind`` of layer ``L`` on the side stream."""
-        ranges = [(t, b) for t, b in L.warm.get(kind, []) if b > 0]
-        if not ranges:
-            return
-        main = torch.cuda.current_stream(self.device)
-        if self._side is None:
-            self._side = torch.cuda.Stream(self.device)
-        self._side.wait_stream(main)  # starts when the kernel before this launch is done
-        with torch.cuda.stream(self._side):
-            kernels.l2_prefetch(ranges, ctas=16, device=self.device)
 
     @torch.inference_mode()
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, bits: torch.Tensor, offset: int = 0,
@@ -405,7 +348,6 @@ class FusedTarget:
         cap = self.cache.capacity
         splits = self._splits(n)
         res, xn = self.residual[:n], self.xnorm[:n]
-        warm = self._warm if self.l2_stream else (lambda L, kind: None)
         if self.peer is not None:
             self.peer.step()
         for L in self.layers:
@@ -416,20 +358,16 @@ class FusedTarget:
                 j = capture.get(L.index - 1)
                 if j is not None:
                     self.hidden_out[:n, j * hid: (j + 1) * hid].copy_(res)
-            warm(L, "qkv")
             self._qkv(L, xn, positions, offset, offset_dev)
             kc, vc = slab[2 * L.index], slab[2 * L.index + 1]
-            warm(L, "attn")
             # this rank's heads go straight into its exchange slot under the peer exchange
             attn_out = self.attn[:n] if self.peer is None else self.peer.slot(L.index, n).view(n, L.hq, -1)
             if offset_dev is not None:
                 kernels.tree_attention(self.q[:n], kc, vc, bits, cap - n, scale=L.scale, out=attn_out,
-                                       num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap,
-                                       l2_prefetch=L.l2pf)
+                                       num_splits=splits, prefix_len_dev=offset_dev, kv_capacity=cap)
             else:
                 kernels.tree_attention(self.q[:n], kc[:, : offset + n], vc[:, : offset + n], bits, offset,
-                                       scale=L.scale, out=attn_out, num_splits=splits, kv_capacity=cap,
-                                       l2_prefetch=L.l2pf)
+                                       scale=L.scale, out=attn_out, num_splits=splits, kv_capacity=cap)
             attn = attn_out
             fused_pull = False
             if self.peer is not None:
@@ -441,15 +379,12 @@ class FusedTarget:
             elif L.split is not None:
                 group, world, _ = L.split
                 attn = gather_heads(attn.unsqueeze(0), group, world)[0]
-            warm(L, "o")
             if fused_pull:
                 self.peer.linear(L.index, n, L.o_w, self.o[:n])
             else:
                 self._linear(attn.reshape(n, -1), L.o_w, L.o_b, self.o[:n], kind="o")
             kernels.add_rmsnorm(self.o[:n], res, L.post_norm, L.eps_post, xn)
-            warm(L, "gate_up")
             self._linear(xn, L.gate_up_w, None, self.act[:n], epilogue=1, kind="gate_up")
-            warm(L, "down")
             self._linear(self.act[:n], L.down_w, None, self.mlp_out[:n], kind="down")
         kernels.add_rmsnorm(self.mlp_out[:n], res, self.final_norm, self.eps, xn)
         j = capture.get(last)
@@ -462,6 +397,4 @@ class FusedTarget:
             self.last_posterior = kernels.linear_argmax(xn, self.lm_head, logits, self.posterior[:n])
         else:
             logits = self._linear(xn, self.lm_head, None, self.logits[:n], kind="lm_head")
-        if self._side is not None:
-            torch.cuda.current_stream(self.device).wait_stream(self._side)  # rejoin (graph capture needs it)
         return logits

@@ -100,15 +100,6 @@ def pdl_enabled() -> bool:
     return bool(_lib.load().rt_pdl_enabled())
 
 
-def set_linear_weight_warm(enabled: bool) -> None:
-    """rt_linear launches ask the L2 for each CTA's weight rows at entry (rt_set_linear_weight_warm)."""
-    _lib.load().rt_set_linear_weight_warm(int(bool(enabled)))
-
-
-def linear_weight_warm_enabled() -> bool:
-    return bool(_lib.load().rt_linear_weight_warm_enabled())
-
-
 def status_tensor(device) -> torch.Tensor:
     """The device status word the kernels of this process report into."""
     return _STATE.status(device)
@@ -207,15 +198,12 @@ def _as3(t: torch.Tensor) -> torch.Tensor:
 def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits: torch.Tensor, prefix_len: int,
                    scale: float | None = None, out: torch.Tensor | None = None, num_splits: int = 0,
                    path: int = 0, prefix_len_dev: torch.Tensor | None = None,
-                   kv_capacity: int | None = None, l2_prefetch=None) -> torch.Tensor:
+                   kv_capacity: int | None = None) -> torch.Tensor:
     """Masked GQA attention of n tree nodes over ``[prefix ; tree block]``.
 
     q: ``[n, Hq, D]`` or HF's ``[1, Hq, n, D]``; k, v: ``[Hkv, S, D]`` or
     ``[1, Hkv, S, D]`` (rows ``[0, prefix_len + n)`` are used);
     mask_bits: int32 ``[n, W]`` ancestor bits of the tree block.
-    ``l2_prefetch``: up to 16 ``(tensor, nbytes)`` ranges (device memory the
-    next kernels read, e.g. their weights) that the launch asks the L2 to load
-    while it runs (rt_tree_attn_ex); results do not depend on it.
     Returns ``out`` ``[n, Hq, D]`` bf16 (HF's ``[1, n, Hq, D]`` after unsqueeze).
     """
     lib = _lib.load()
@@ -243,41 +231,14 @@ def tree_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask_bits:
     splits, merged = attn_plan(n, hq, hkv, int(prefix_len), num_splits, path)
     ws_bytes = 0 if merged else lib.rt_tree_attn_workspace_size(n, hq, hkv, d, int(prefix_len), splits)
     ws = _STATE.buffer(q.device, "attn_ws", ws_bytes) if ws_bytes else None
-    pf = _l2_ranges(l2_prefetch) if l2_prefetch else None
-    rc = lib.rt_tree_attn_ex(q.data_ptr(), q.stride(0) * es, q.stride(1) * es, k.data_ptr(), v.data_ptr(),
-                             k.stride(0) * es, k.stride(1) * es, cap, out.data_ptr(), out.stride(0) * es,
-                             out.stride(1) * es, mask_bits.data_ptr(), words, n, int(prefix_len),
-                             _ptr(prefix_len_dev), hq, hkv, d, scale, splits, path, _ptr(ws), ws_bytes,
-                             None if pf is None else ctypes.addressof(pf), _STATE.status(q.device).data_ptr(),
-                             _stream(q.device))
+    rc = lib.rt_tree_attn(q.data_ptr(), q.stride(0) * es, q.stride(1) * es, k.data_ptr(), v.data_ptr(),
+                          k.stride(0) * es, k.stride(1) * es, cap, out.data_ptr(), out.stride(0) * es,
+                          out.stride(1) * es, mask_bits.data_ptr(), words, n, int(prefix_len),
+                          _ptr(prefix_len_dev), hq, hkv, d, scale, splits, path, _ptr(ws), ws_bytes,
+                          _STATE.status(q.device).data_ptr(), _stream(q.device))
     _lib.check(rc, "rt_tree_attn")
     _count(2 if ws_bytes else 1)  # the combine launch runs only when the partials go through the workspace
     return out
-
-
-def _l2_ranges(ranges) -> "_lib.L2Ranges":
-    """``rt_l2_ranges`` from ``(tensor, nbytes)`` pairs: the first ``nbytes`` of each contiguous CUDA tensor."""
-    if len(ranges) > _lib.RT_L2_MAX_RANGES:
-        raise ValueError(f"at most {_lib.RT_L2_MAX_RANGES} L2 ranges")
-    r = _lib.L2Ranges()
-    r.count = len(ranges)
-    for i, (t, nbytes) in enumerate(ranges):
-        _require_cuda(t)
-        if not t.is_contiguous():
-            raise RuntimeError("an L2 range must be a contiguous tensor")
-        r.ptr[i] = t.data_ptr()
-        r.bytes[i] = max(0, min(int(nbytes), t.numel() * t.element_size()))
-    return r
-
-
-def l2_prefetch(ranges, ctas: int = 16, device=None) -> None:
-    """Ask the L2 to load ``(tensor, nbytes)`` ranges (rt_l2_prefetch on the current stream); nothing waits."""
-    if not ranges:
-        return
-    pf = _l2_ranges(ranges)
-    dev = ranges[0][0].device if device is None else device
-    _lib.check(_lib.load().rt_l2_prefetch(ctypes.addressof(pf), int(ctas), _stream(dev)), "rt_l2_prefetch")
-    _count()
 
 
 def attn_plan(n: int, num_q_heads: int, num_kv_heads: int, prefix_len: int, num_splits: int = 0,
@@ -539,8 +500,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ep
     silu(gate) * up``; 2 (w = [Wq; Wk; Wv]): head norms + rotary, q to
     ``qkv['q_out']``, k/v into the cache (keys of ``qkv`` as in
     ``qk_norm_rope_append``: num_q_heads, num_kv_heads, q_norm, k_norm, eps,
-    cos, sin, positions, q_out, k_cache, v_cache, offset, offset_dev); 3: as 2,
-    and the launch warms the L2 with the cache's K/V prefix rows.
+    cos, sin, positions, q_out, k_cache, v_cache, offset, offset_dev).
     """
     lib = _lib.load()
     _require_cuda(x, w, out)
@@ -557,7 +517,7 @@ def linear(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, ep
         raise RuntimeError(f"rt_linear does not take m={m}, n_out={n_out}, k={k}")
     epi = None
     keep = []
-    if epilogue in (_lib.RT_EPI_QKV_ROPE, _lib.RT_EPI_QKV_ROPE_KV_WARM):
+    if epilogue == _lib.RT_EPI_QKV_ROPE:
         kc, vc = qkv["k_cache"], qkv["v_cache"]
         es = kc.element_size()
         epi = _lib.QkvEpilogue(qkv["num_q_heads"], qkv["num_kv_heads"], _ptr(qkv.get("q_norm")),

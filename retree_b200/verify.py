@@ -58,9 +58,8 @@ def extract_context_feature(hidden_states, layer_ids):
 class TreeVerifier:
     def __init__(self, target, tree_budget: int, max_length: int, draft_horizon: int = 15,
                  temperature: float = 0.0, target_layer_ids=None, device=None, fused: bool | None = None,
-                 gemm: str = "auto", fused_draft: bool = False, attn_l2_prefetch: int | None = None,
-                 l2_stream: bool | None = None, exchange: str = "nccl", chain: bool = False,
-                 fused_argmax: bool = False, kv_l2_prefetch: bool | None = None):
+                 gemm: str = "auto", fused_draft: bool = False, exchange: str = "nccl", chain: bool = False,
+                 fused_argmax: bool = False):
         cfg = target.config
         if getattr(cfg, "_attn_implementation", None) not in (ATTN_NAME, HEADSPLIT_NAME):
             raise RuntimeError(f"target must use attn_implementation={ATTN_NAME!r} (retree_b200.attention.register())")
@@ -125,10 +124,8 @@ class TreeVerifier:
             fused = (target_layer_ids is None and fused_mod.supports(target)
                      and not hasattr(target, "_rt_local_kv_heads"))
         self.fused = (fused_mod.FusedTarget(target, self.cache, self.n_max, gemm=gemm,
-                                            capture_layers=target_layer_ids, attn_l2_prefetch=attn_l2_prefetch,
-                                            l2_stream=l2_stream, exchange=exchange,
-                                            argmax=fused_argmax and self.temperature < 1e-5,
-                                            kv_l2_prefetch=kv_l2_prefetch)
+                                            capture_layers=target_layer_ids, exchange=exchange,
+                                            argmax=fused_argmax and self.temperature < 1e-5)
                       if fused else None)
         # draft forward: the DFlash module (reference layout) on the fused stages
         # (retree_b200.draft.FusedDraft) when asked for and supported

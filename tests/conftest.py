@@ -20,7 +20,7 @@ def golden_dir():
 
 # late test files, in the order they run (the hot path's next rows first); late files not listed run after
 LATE_ORDER = ("test_recovery_walk_gpu", "test_linear_argmax_gpu", "test_wait_timeouts_gpu", "test_peer_gpu",
-              "test_l2_prefetch_gpu", "test_draft_gpu")
+              "test_draft_gpu")
 
 
 def _module(item) -> str:

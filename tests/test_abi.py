@@ -95,35 +95,11 @@ def test_linear_shape_checks_without_gpu():
                          (256, 128), (384, 256), (1536, 512)):
             for epi in (0, 1):
                 assert lib.rt_linear_check(m, n_out, k, epi) == 0, (m, n_out, k, epi)
-    assert lib.rt_linear_check(17, 6144, 2560, 3) == 0  # QKV epilogue with the K/V prefix warm-up
-    assert lib.rt_linear_check(17, 6144, 2560, 4) != 0
+    assert lib.rt_linear_check(17, 6144, 2560, 2) == 0  # QKV epilogue
+    assert lib.rt_linear_check(17, 6144, 2560, 3) != 0
     assert lib.rt_linear_check(513, 128, 64, 0) != 0
     assert lib.rt_linear_check(17, 200, 64, 0) != 0
     assert lib.rt_linear_check(17, 256, 60, 0) != 0
-
-
-def test_l2_prefetch_struct_and_checks_without_gpu():
-    import ctypes
-    assert ctypes.sizeof(_lib.L2Ranges) == 8 + 16 * 8 + 16 * 8 and _lib.L2Ranges.bytes.offset == 136
-    lib = _lib.load()
-    pf = _lib.L2Ranges()
-    pf.count = 1
-    pf.ptr[0], pf.bytes[0] = 4096 + 8, 1 << 20  # not 16-byte aligned: refused before any launch
-    fake = 1 << 20  # aligned addresses that the host side never dereferences
-    rc = lib.rt_tree_attn_ex(fake, 32 * 256, 256, fake, fake, 4096 * 256, 256, 4096, fake, 32 * 256, 256, fake, 1,
-                             17, 2048, None, 32, 8, 128, 1.0, 1, 0, None, 0, ctypes.addressof(pf), None, None)
-    assert rc == _lib.RT_ERR_INVALID_ARGUMENT
-    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 4, None) == _lib.RT_ERR_INVALID_ARGUMENT
-    pf.count = 17
-    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 4, None) == _lib.RT_ERR_INVALID_ARGUMENT
-    pf.count = 0
-    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 0, None) == _lib.RT_ERR_INVALID_ARGUMENT
-    assert lib.rt_l2_prefetch(ctypes.addressof(pf), 4, None) == _lib.RT_OK  # nothing to request
-    with pytest.raises(RuntimeError, match="CUDA"):
-        kernels.tree_attention(torch.zeros(17, 32, 128), torch.zeros(8, 64, 128), torch.zeros(8, 64, 128),
-                               torch.zeros(17, 1, dtype=torch.int32), 40, l2_prefetch=[(torch.zeros(64), 256)])
-    with pytest.raises(RuntimeError, match="CUDA"):
-        kernels.l2_prefetch([(torch.zeros(64), 256)])
 
 
 def test_peer_exchange_argument_checks_without_gpu():
@@ -146,36 +122,6 @@ def test_peer_exchange_argument_checks_without_gpu():
     assert lib.rt_peer_epoch_step(None, 1, None) == _lib.RT_ERR_INVALID_ARGUMENT
 
 
-def test_l2_warm_share_arithmetic_stays_inside_each_range():
-    """The per-CTA share / 32 KB piece arithmetic of l2_warm_share (csrc/common.cuh), emulated: every request
-    lies inside its range, is a multiple of 16 bytes, and together the requests cover the range once."""
-    import random
-
-    def requests(nbytes, ctas, parts, piece=32768):
-        per = (((nbytes + ctas - 1) // ctas) + 15) & ~15
-        out = []
-        for c in range(ctas):
-            b0, b1 = c * per, min(nbytes, c * per + per)
-            for part in range(parts):
-                o = b0 + part * piece
-                while o < b1:
-                    out.append((o, min(piece, b1 - o)))
-                    o += parts * piece
-        return out
-
-    rng = random.Random(0)
-    cases = [(16, 1, 30), (48000, 136, 30), (21 << 20, 136, 30), (100 << 20, 16, 32), (96, 148, 32)]
-    cases += [(16 * rng.randint(1, 1 << 22), rng.randint(1, 300), rng.choice((30, 32))) for _ in range(40)]
-    for nbytes, ctas, parts in cases:
-        reqs = sorted(requests(nbytes, ctas, parts))
-        assert all(o % 16 == 0 and n % 16 == 0 and n > 0 and o + n <= nbytes for o, n in reqs), (nbytes, ctas)
-        pos = 0
-        for o, n in reqs:
-            assert o == pos, (nbytes, ctas, parts)
-            pos += n
-        assert pos == nbytes
-
-
 def test_a_plain_c_host_compiles_links_and_calls_the_abi(tmp_path):
     """include/retree_b200.h is C11 (pedantic, warnings as errors), and a C program links the library and
     calls its host-only entry points (no GPU needed for these)."""
@@ -192,8 +138,6 @@ def test_a_plain_c_host_compiles_links_and_calls_the_abi(tmp_path):
 #include <stdio.h>
 #include "retree_b200.h"
 int main(void) {
-  rt_l2_ranges r = {0};
-  (void)r;
   printf("%d %s %zu %d\n", rt_abi_version(), rt_status_string(RT_ERR_INVALID_ARGUMENT),
          rt_tree_attn_workspace_size(17, 32, 8, 128, 2048, 17), rt_linear_check(17, 2560, 4096, RT_EPI_STORE));
   return 0;
@@ -206,13 +150,6 @@ int main(void) {
     want_ws = _lib.load().rt_tree_attn_workspace_size(17, 32, 8, 128, 2048, 17)
     assert out[0] == "2" and " ".join(out[1:-2]) == "invalid argument"
     assert int(out[-2]) == want_ws > 0 and out[-1] == "0"
-
-
-def test_launch_switches_without_gpu():
-    kernels.set_linear_weight_warm(True)
-    assert kernels.linear_weight_warm_enabled()
-    kernels.set_linear_weight_warm(False)
-    assert not kernels.linear_weight_warm_enabled()
 
 
 def test_integration_ctypes_stub_matches_the_library():

@@ -68,7 +68,7 @@ def fake_kernels(monkeypatch):
         return q_out
 
     def tree_attention(q, k, v, bits, prefix_len, scale=None, out=None, num_splits=0, path=0, prefix_len_dev=None,
-                       kv_capacity=None, l2_prefetch=None):
+                       kv_capacity=None):
         if q.dim() == 4:  # HF's [1, Hq, n, D] / [1, Hkv, S, D], as the real wrapper takes them
             q, k, v = q[0].transpose(0, 1), k[0], v[0]
         n, hq, d = q.shape
@@ -185,34 +185,6 @@ def test_fused_target_layer_capture_plumbing(fake_kernels):
         got = ft.hidden_out[:n, j * h: (j + 1) * h].float()
         assert float((got - want).norm() / want.norm()) < 2e-2, li
     assert float((logits.float() - out.logits[0].float()).norm() / out.logits[0].float().norm()) < 2e-2
-
-
-@torch.inference_mode()
-def test_side_stream_warm_up_plan(fake_kernels):
-    """The L2 warm-up plan: next to each launch, the weights of the projection after it, within the budget."""
-    from transformers import Qwen3Config, Qwen3ForCausalLM
-
-    cfg = Qwen3Config(vocab_size=300, hidden_size=256, intermediate_size=512, num_hidden_layers=2,
-                      num_attention_heads=4, num_key_value_heads=2, head_dim=128, tie_word_embeddings=False)
-    cfg._attn_implementation = "sdpa"
-    model = Qwen3ForCausalLM(cfg).to(BF).eval()
-    budget = 300_000
-    ft = fused_mod.FusedTarget(model, FakeCache(2, 2, 128, 64), n_max=8, gemm="cublas", l2_stream=True,
-                               l2_stream_budget=budget, attn_l2_prefetch=0)
-    nb = lambda t: t.numel() * t.element_size()  # noqa: E731
-    L0, L1 = ft.layers
-    assert L0.warm["qkv"] == [(L0.o_w, min(nb(L0.o_w), budget))]
-    (t, b), = L0.warm["attn"]
-    assert t is L0.gate_up_w and b == budget
-    (rest, b2), = L0.warm["o"]
-    assert rest.is_contiguous() and rest.data_ptr() == L0.gate_up_w.data_ptr() + budget // (2 * 256) * 512
-    assert b2 == min(nb(L0.gate_up_w) - budget, budget)
-    assert L0.warm["gate_up"][0][0] is L0.down_w and L0.warm["down"][0][0] is L1.qkv_w
-    assert L1.warm["down"][0][0] is ft.lm_head
-    for L in ft.layers:
-        for ranges in L.warm.values():
-            for t, b in ranges:
-                assert 0 < b <= min(budget, nb(t)) and t.is_contiguous()
 
 
 @torch.inference_mode()
