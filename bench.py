@@ -338,12 +338,17 @@ def run_ours(args, wl, rank, world, local_rank):
         # one row of DELTA_PAIRS * 3 int32 per rank, carried as bf16 columns; two slots by step parity
         delta_peer = PeerExchange(None, rank, world, 1, DELTA_PAIRS * 3 * 2, 2, dev)
     n_exchanges = [0]
+    pending = [None]
 
     def exchange():
         if world <= 1 or wl.get("split"):
             return
         if delta_peer is None:
-            dist.all_gather_into_tensor(delta_recv.view(world * DELTA_PAIRS, 3), delta_send)
+            # issued on NCCL's stream without a wait, so it overlaps the next round's
+            # replay; the previous step's gather is waited for before its buffer is reused
+            settle()
+            pending[0] = dist.all_gather_into_tensor(delta_recv.view(world * DELTA_PAIRS, 3), delta_send,
+                                                     async_op=True)
             return
         slot = n_exchanges[0] % 2
         if slot == 0:
@@ -353,7 +358,14 @@ def run_ours(args, wl, rank, world, local_rank):
         delta_peer.gather(slot, 1, delta_recv.view(1, -1).view(torch.bfloat16))
         n_exchanges[0] += 1
 
+    def settle():
+        # the current stream waits for the last step's delta gather
+        if pending[0] is not None:
+            pending[0].wait()
+            pending[0] = None
+
     def barrier():
+        settle()
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -387,6 +399,7 @@ def run_ours(args, wl, rank, world, local_rank):
         for i in range(steps):
             accepted.append(v.round(resident[warm + i]))
             exchange()
+        settle()
         ev1.record()
         torch.cuda.nvtx.range_pop()
 
@@ -462,6 +475,7 @@ def run_ours(args, wl, rank, world, local_rank):
             acc = v2.round(logits)
             out_host[: acc + 1].copy_(v2.output_ids[s0: s0 + acc + 1])
             exchange()
+        settle()
         e1.record()
 
     timed(rounds_e2e)
