@@ -19,7 +19,7 @@
 
 namespace rt {
 
-constexpr int kBuildThreads = 256;
+constexpr int kBuildThreads = 1024;  // the prologue's table build; the expansion is warp 0
 constexpr int kMaxTail = 7;        // max_n - 1 for max_n <= 8
 constexpr int kMaxRows = 64;       // depth limit (draft rows)
 constexpr int kMaxBudget = 1024;
@@ -280,26 +280,27 @@ __global__ void __launch_bounds__(kBuildThreads) tree_build_kernel(BuildArgs a) 
   // beta * min(sum_n w^(n-2) * log1p(count_n), cap) of up to two queries at once
   // (ddtree.py:154-186, :412-420): query 0 on lanes 0..15 (one lane per order),
   // query 1 on lanes 16..31; every lane returns both results.
+  // this lane's order weight longer_weight^(n-2) for n = (lane % 16) + 2
+  const double lane_ow = (lane & 15) < kMaxTail ? a.ow[lane & 15] : 0.0;
   auto bonus_pair = [&](const int* t0, int64_t tok0, bool on0, const int* t1, int64_t tok1, bool on1,
                         double& inc0, double& inc1) {
     const bool q1 = lane >= 16;
     const int* tl_ptr = q1 ? t1 : t0;
     const int p = (lane & 15) + 1;
+    const bool order_on = p <= tail_size && p <= tl_ptr[7];
     int c = 0;
-    if ((q1 ? on1 : on0) && p <= tail_size && p <= tl_ptr[7])
+    if ((q1 ? on1 : on0) && order_on)
       c = ngram_count(table, hmask, ctx, tl_ptr, tl_ptr[7], p, static_cast<int>(q1 ? tok1 : tok0));
-    // each lane fetches its own order's log1p(count), so the loads overlap
+    // each lane forms its own order's term w^(n-2) * log1p(count) (0 where the
+    // reference adds nothing: adding +0.0 to the non-negative sum changes no bit)
     const int ci = min(c, a.table_len - 1);
     const double base = !a.use_log_count ? 1.0 : (ci < a.log1p_staged ? s_log1p[ci] : a.log1p_table[ci]);
-    const int tla = t0[7], tlb = t1[7];
+    const double term = (order_on && c >= a.min_count) ? __dmul_rn(lane_ow, base) : 0.0;
+    // summed over n = 2..max_n in ascending order, as the reference adds them
     double sa = 0.0, sb = 0.0;
     for (int n = 2; n <= a.max_n; ++n) {
-      const int ca = __shfl_sync(0xFFFFFFFFu, c, n - 2);
-      const int cb = __shfl_sync(0xFFFFFFFFu, c, 16 + n - 2);
-      const double ba = __shfl_sync(0xFFFFFFFFu, base, n - 2);
-      const double bb = __shfl_sync(0xFFFFFFFFu, base, 16 + n - 2);
-      if (tla >= n - 1 && ca >= a.min_count) sa = __dadd_rn(sa, __dmul_rn(a.ow[n - 2], ba));
-      if (tlb >= n - 1 && cb >= a.min_count) sb = __dadd_rn(sb, __dmul_rn(a.ow[n - 2], bb));
+      sa = __dadd_rn(sa, __shfl_sync(0xFFFFFFFFu, term, n - 2));
+      sb = __dadd_rn(sb, __shfl_sync(0xFFFFFFFFu, term, 16 + n - 2));
     }
     if (a.max_bonus > 0.0) {
       sa = (a.max_bonus < sa) ? a.max_bonus : sa;
@@ -332,42 +333,58 @@ __global__ void __launch_bounds__(kBuildThreads) tree_build_kernel(BuildArgs a) 
     // ---- arg-max: (score desc, then the heap tuple's tie order) ----
     double bs = -INFINITY;
     uint32_t bk = kNoCand;  // (parent << 21) | (rank << 11) | slot
-    for (int e = lane; e < nfront; e += 32) {
-      const double s = f_aug[e];
-      const uint32_t key = (static_cast<uint32_t>(f_parent[e]) << 21) | (static_cast<uint32_t>(f_rank[e]) << 11) |
-                           static_cast<uint32_t>(e);
-      bool take = bk == kNoCand || s > bs;
-      if (!take && s == bs) {
-        if (heap_order) {
+    if (!heap_order) {
+      // n-gram heaps: tuples (-aug, parent, rank), so the winner is the largest
+      // score, then the smallest (parent, rank).  Scores become order-preserving
+      // 64-bit keys (-0.0 as +0.0, equal doubles equal keys) and the warp
+      // reduces them with three redux operations instead of a shuffle tree.
+      uint64_t bo = 0;
+      for (int e = lane; e < nfront; e += 32) {
+        const double s = f_aug[e];
+        const int64_t bits = s == 0.0 ? 0 : __double_as_longlong(s);
+        const uint64_t o = bits < 0 ? ~static_cast<uint64_t>(bits) : (static_cast<uint64_t>(bits) | (1ull << 63));
+        const uint32_t key = (static_cast<uint32_t>(f_parent[e]) << 21) | (static_cast<uint32_t>(f_rank[e]) << 11) |
+                             static_cast<uint32_t>(e);
+        if (bk == kNoCand || o > bo || (o == bo && key < bk)) {
+          bo = o;
+          bk = key;
+        }
+      }
+      const uint32_t hi = static_cast<uint32_t>(bo >> 32), lo = static_cast<uint32_t>(bo);
+      const uint32_t m_hi = __reduce_max_sync(0xFFFFFFFFu, hi);
+      const uint32_t m_lo = __reduce_max_sync(0xFFFFFFFFu, hi == m_hi ? lo : 0u);
+      const bool top = bk != kNoCand && hi == m_hi && lo == m_lo;
+      bk = __reduce_min_sync(0xFFFFFFFFu, top ? bk : kNoCand);
+    } else {
+      for (int e = lane; e < nfront; e += 32) {
+        const double s = f_aug[e];
+        const uint32_t key = (static_cast<uint32_t>(f_parent[e]) << 21) | (static_cast<uint32_t>(f_rank[e]) << 11) |
+                             static_cast<uint32_t>(e);
+        bool take = bk == kNoCand || s > bs;
+        if (!take && s == bs) {
           const int eb = bk & 0x7FF;
           take = path_less(n_rank, n_parent, f_parent[e], f_rank[e], f_depth[e], f_parent[eb], f_rank[eb],
                            f_depth[eb]);
-        } else {
-          take = key < bk;
+        }
+        if (take) {
+          bs = s;
+          bk = key;
         }
       }
-      if (take) {
-        bs = s;
-        bk = key;
-      }
-    }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const double os = __shfl_xor_sync(0xFFFFFFFFu, bs, o);
-      const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
-      bool take = ok != kNoCand && (bk == kNoCand || os > bs);
-      if (!take && ok != kNoCand && os == bs) {
-        if (heap_order) {
+      for (int o = 16; o > 0; o >>= 1) {
+        const double os = __shfl_xor_sync(0xFFFFFFFFu, bs, o);
+        const uint32_t ok = __shfl_xor_sync(0xFFFFFFFFu, bk, o);
+        bool take = ok != kNoCand && (bk == kNoCand || os > bs);
+        if (!take && ok != kNoCand && os == bs) {
           const int ea = ok & 0x7FF, eb = bk & 0x7FF;
           take = path_less(n_rank, n_parent, f_parent[ea], f_rank[ea], f_depth[ea], f_parent[eb], f_rank[eb],
                            f_depth[eb]);
-        } else {
-          take = ok < bk;
         }
-      }
-      if (take) {
-        bs = os;
-        bk = ok;
+        if (take) {
+          bs = os;
+          bk = ok;
+        }
       }
     }
     if (bk == kNoCand) break;
