@@ -58,7 +58,11 @@ constexpr uint32_t kOffStage = 0;
 constexpr uint32_t kOffMl = 2 * kTile;
 constexpr uint32_t kOffWeights = 3 * kTile;  // [owned rows][kMaxMerge] fp32 merge weights
 constexpr int kMaxMerge = 16;  // cluster size limit (16 needs the non-portable cluster attribute)
-constexpr uint32_t kTmemCols = 512;                   // S0 | S1 | O | spare
+constexpr uint32_t kTmemCols = 512;                   // S0 | S1 | O | P0 P1
+// P_b (bf16, two keys per 32-bit column, row r in lane r) at TMEM columns
+// kPCol + 64*b: the A operand of the PV product, read by the tensor core
+// straight from TMEM.
+constexpr uint32_t kPCol = 3 * 128;
 constexpr float kRescaleThreshold = 8.0f;             // log2 units
 
 struct AttnParams {
@@ -434,15 +438,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                mbar_wait(&bar.full_v[pb], pph, abort_flag, p.status, RT_DEV_WAIT_TIMEOUT);
           if (!ok) break;
           tc_fence_after();
-          const uint32_t sp = smem_u32(smem + kOffP + pb * kTile);
           const uint32_t sv = smem_u32(smem + kOffV + pb * kTile);
 #pragma unroll
           for (int kk = 0; kk < kBN / 16; ++kk) {
-            const uint32_t poff = (kk >> 2) * kHalf + (kk & 3) * 32;
-            // V is MN-major: 16 keys = two 8-row SW128 atoms (1024 B apart);
-            // the second 64-column half of head_dim sits one box (LBO) away.
-            umma_f16(tmem + 2 * kBN, smem_desc_sw128(sp + poff, 16, 1024),
-                     smem_desc_sw128(sv + kk * 2048, kHalf, 1024), idesc_pv, (jp > 0 || kk > 0) ? 1u : 0u);
+            // P from TMEM: 16 keys = 8 packed columns.  V is MN-major: 16 keys =
+            // two 8-row SW128 atoms (1024 B apart); the second 64-column half
+            // of head_dim sits one box (LBO) away.
+            umma_f16_ts(tmem + 2 * kBN, tmem + kPCol + pb * 64 + kk * 8,
+                        smem_desc_sw128(sv + kk * 2048, kHalf, 1024), idesc_pv, (jp > 0 || kk > 0) ? 1u : 0u);
           }
           umma_commit(&bar.o_done[pb]);
           umma_commit(&bar.empty_v[pb]);
@@ -551,29 +554,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         mbar_arrive(&bar.p_full[b]);
         continue;
       }
-      // P = exp2(s*scale - m): exp2 on packed f16 pairs, sum in fp32, stored as
-      // bf16 in this half's SW128 K-major box of the P tile
+      // P = exp2(s*scale - m), summed in fp32, stored as bf16 pairs into this
+      // half's 32 columns of the TMEM P buffer (keys 2i, 2i+1 in column i)
       float ls[4] = {0.f, 0.f, 0.f, 0.f};
-      unsigned char* pbuf = smem + kOffP + b * kTile + half * kHalf;
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {
+        uint32_t pk[16];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {  // 8 keys = one 16-byte chunk
-          uint32_t pk[4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float p0 = ex2(fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t]), sl2, -mu));
-            const float p1 = ex2(fmaf(__uint_as_float(sreg[c2][q * 8 + 2 * t + 1]), sl2, -mu));
-            ls[t] += p0 + p1;
-            pk[t] = pack_bf16x2(p0, p1);
-          }
-          const int ch = c2 * 4 + q;  // 16-byte chunk within the 128-byte row
-          const uint32_t off = r * 128 + ((ch ^ (r & 7)) << 4);
-          *reinterpret_cast<uint4*>(pbuf + off) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(fmaf(__uint_as_float(sreg[c2][2 * i]), sl2, -mu));
+          const float p1 = ex2(fmaf(__uint_as_float(sreg[c2][2 * i + 1]), sl2, -mu));
+          ls[i & 3] += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
         }
+        tmem_st16(tmem + lane_base + kPCol + b * 64 + half * 32 + c2 * 16, pk);
       }
       l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-      fence_proxy_async_smem();
+      tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar.p_full[b]);
     }
