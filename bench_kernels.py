@@ -2,6 +2,7 @@
 
     python bench_kernels.py sweep  [--prefix 4096] [--budgets 16,32,64,128,256] [--layers 36]
     python bench_kernels.py single --budget 16 --prefix 2048 [--reps 3]
+    python bench_kernels.py topk --budget 16 [--reps 3]
     python bench_kernels.py parts
     python bench_kernels.py linear [--m 17,65,257] [--shapes qkv,o,gate_up,down,lm_head]
 
@@ -12,7 +13,8 @@ layer so consecutive launches stream from HBM (36 x (L+n) x 4 KiB > L2), all
 layers captured in one CUDA graph and timed with CUDA events.  Each line
 reports the algorithmic bytes and FLOPs per launch, the achieved GB/s and
 TFLOP/s, and both as fractions of the measured peaks (MEASURED_PEAKS.json).
-``single`` runs a few launches of one shape (for ncu captures); ``parts``
+``single`` runs a few launches of one shape (for ncu captures), ``topk`` a
+few draft top-k calls on the bench workload's logits (the same); ``parts``
 times the draft top-k, the tree build and the compaction kernels; ``linear``
 times rt_linear against cuBLAS on the Qwen3-4B projection shapes (36 weight
 copies per graph, so every launch streams its weights from HBM).
@@ -217,7 +219,7 @@ def draft_case(dev, hidden: int = 4096, layers: int = 5, ctx: int = 5, prefix: i
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("mode", choices=("sweep", "single", "parts", "linear", "draft"))
+    ap.add_argument("mode", choices=("sweep", "single", "topk", "parts", "linear", "draft"))
     ap.add_argument("--m", default="17,65,257")
     ap.add_argument("--shapes", default="qkv,o,gate_up,down,lm_head")
     ap.add_argument("--prefix", type=int, default=4096)
@@ -242,6 +244,13 @@ def main():
         torch.cuda.synchronize()
         kernels.check_device_status(dev)
         print(json.dumps(dict(ok=True, budget=a.budget, prefix=a.prefix)))
+    elif a.mode == "topk":
+        # a few calls of the draft top-k on the bench workload's logits (for ncu captures)
+        logits = torch.from_numpy(synthetic.draft_logits(0, 16, 151936)[-15:]).to(dev).to(torch.bfloat16)
+        for _ in range(a.reps):
+            kernels.draft_topk(logits, a.budget)
+        torch.cuda.synchronize()
+        print(json.dumps(dict(ok=True, budget=a.budget, rows=15, vocab=151936)))
     elif a.mode == "draft":
         for row in draft_case(dev, prefix=a.prefix):
             print(json.dumps(row), flush=True)
