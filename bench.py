@@ -112,7 +112,7 @@ def measured_peaks():
 # of the current kernel at the workload's live shape: workload -> (bytes, prefix_len, tree_nodes, how taken).
 # Scaled to the live prefix by the K/V bytes per key when the bench's prefix differs.
 ATTN_TRAFFIC = {
-    "qwen3-4b-b16": (8785920, 2075, 17, "ncu dram__bytes_read.sum + dram__bytes_write.sum of one tree_attn_tc_kernel "
+    "qwen3-4b-b16": (8776704, 2075, 17, "ncu dram__bytes_read.sum + dram__bytes_write.sum of one tree_attn_tc_kernel "
                      "launch, cold L2 (bench_kernels.py single --budget 16 --prefix 2075)"),
 }
 
