@@ -439,10 +439,15 @@ int sm_count() {
   return n;
 }
 
-// 64-column K blocks per ring stage.  One: two and four (longer contiguous
-// runs of each weight row per stage) measured no faster at tree sizes and cost
-// the two-CTAs-per-SM configurations their ring depth.
-int linear_bps() { return 1; }
+// 64-column K blocks per ring stage.  Where the 128-row tiles do not cover
+// the SMs (K split over a cluster, one CTA per SM) a stage takes kSplitBps
+// blocks: fewer, longer transfers per weight row and fewer ring round trips
+// (measured at 17 rows: down_proj 18.1 -> 14.5 us with two blocks, 13.8 with
+// four; the ring depth itself, 8 or 12 one-block stages, made no difference).
+// Where the tiles cover the SMs a stage takes one block, so two CTAs share an
+// SM with a ring each.
+constexpr int kSplitBps = 4;
+int linear_bps(int tiles, int chunks) { return (chunks == 1 && tiles < sm_count()) ? kSplitBps : 1; }
 
 // CTAs (clusters of `cluster`) of linear_kernel that fit on the GPU at once
 // with `smem` bytes each (cached per shape of the launch).
@@ -487,7 +492,7 @@ int make_plan(int m, int n_out, int k, int epi, Plan* pl, bool choose) {
   const uint32_t fixed = sizeof(LinBars) + 1024;
   const uint32_t block_bytes = kWTileBytes + static_cast<uint32_t>(pl->chunks * pl->chunk_rows * 128);
   // K blocks per stage: as many as the preference allows with >= 2 stages in 200 KB
-  pl->bps = linear_bps();
+  pl->bps = linear_bps(n_out / 128, pl->chunks);
   while (pl->bps > 1 && 2 * pl->bps * block_bytes > 200u * 1024u) pl->bps >>= 1;
   pl->kblocks = (k + kBK * pl->bps - 1) / (kBK * pl->bps);
   pl->tiles = n_out / 128;
