@@ -48,8 +48,7 @@ constexpr uint32_t kHalf = kTile / 2;      // one 128-row x 64-column SW128 box
 constexpr uint32_t kOffQ = 0;
 constexpr uint32_t kOffK = kTile;           // 2 stages
 constexpr uint32_t kOffV = 3 * kTile;       // 2 stages
-constexpr uint32_t kOffP = 5 * kTile;       // 2 buffers
-constexpr uint32_t kOffBar = 7 * kTile;
+constexpr uint32_t kOffBar = 5 * kTile;     // (P lives in TMEM)
 constexpr uint32_t kAttnSmem = kOffBar + 1536 + 1024;  // + barriers/exchange + alignment slack
 // In-kernel split merge: once a CTA's last PV product is final, the Q / K / V
 // ring is idle and holds the CTA's unnormalised fp32 O tile (rows of 512 B,
@@ -993,6 +992,9 @@ static AttnPlan plan_attn(int n, int G, int hkv, int64_t prefix_len, int num_spl
   // combine launch costs more than the CTAs it would add; measured on B200:
   // 17 blocks merge faster in a 10-CTA cluster than in 17 workspace splits,
   // 33 blocks run equally, 257 blocks twice as fast in workspace splits).
+  // (The largest such cluster, not the fewest splits with the same most blocks
+  // a CTA takes: a CUDA-graph round plans once for the cache capacity while the
+  // live prefix grows, and fewer splits would leave CTAs more blocks of it.)
   if (c == pl.splits || nblk <= 3 * c) {
     pl.splits = c;
     pl.merge = true;
