@@ -2,8 +2,8 @@
 
 TEST INFRASTRUCTURE ONLY. This package is a CPU restatement (numpy / plain
 Python, torch CPU only for the fp32 attention reference) of the reference
-algorithms on the verification hot path of Adamlong3/ReTree. It is the checker:
-only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
+algorithms on the verification hot path of Adamlong3/ReTree, used to check the
+kernels: only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
 ``bench.py`` import it. The product (``retree_b200``) never imports, links or
 calls anything here, and has no CPU fallback.
 
