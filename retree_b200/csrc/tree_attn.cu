@@ -554,21 +554,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         continue;
       }
       // P = exp2(s*scale - m), summed in fp32, stored as bf16 pairs into this
-      // half's 32 columns of the TMEM P buffer (keys 2i, 2i+1 in column i)
-      float ls[4] = {0.f, 0.f, 0.f, 0.f};
+      // half's 32 columns of the TMEM P buffer (keys 2i, 2i+1 in column i); the
+      // scale-and-shift and the running sums go two keys per instruction
+      const float2 sc2 = make_float2(sl2, sl2), sh2 = make_float2(-mu, -mu);
+      float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
       for (int c2 = 0; c2 < 2; ++c2) {
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(__uint_as_float(sreg[c2][2 * i]), sl2, -mu));
-          const float p1 = ex2(fmaf(__uint_as_float(sreg[c2][2 * i + 1]), sl2, -mu));
-          ls[i & 3] += p0 + p1;
+          const float2 x = ffma2(make_float2(__uint_as_float(sreg[c2][2 * i]), __uint_as_float(sreg[c2][2 * i + 1])),
+                                 sc2, sh2);
+          const float p0 = ex2(x.x), p1 = ex2(x.y);
+          acc[i & 1] = fadd2(acc[i & 1], make_float2(p0, p1));
           pk[i] = pack_bf16x2(p0, p1);
         }
         tmem_st16(tmem + lane_base + kPCol + b * 64 + half * 32 + c2 * 16, pk);
       }
-      l += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+      l += (acc[0].x + acc[1].x) + (acc[0].y + acc[1].y);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&bar.p_full[b]);
