@@ -114,6 +114,15 @@ def test_topk_bf16_ties_resolve_to_lowest_index(k):
     _check_topk(xb, k, dev, torch.bfloat16)
 
 
+@pytest.mark.parametrize("k", [16, 64])
+def test_topk_fp16_matches_oracle(k):
+    # fp16 logits: keys whose significant bits end at bit 13, decided by two 12-bit digits
+    dev = cuda()
+    x = gc.make_logits(dict(seed=7, rows=15, vocab=151936))
+    xh = torch.from_numpy(x).to(torch.float16).float().numpy()  # exact in fp16, many ties
+    _check_topk(xh, k, dev, torch.float16)
+
+
 def test_topk_small_vocab_and_specials():
     dev = cuda()
     x = np.random.default_rng(3).standard_normal((4, 300)).astype(np.float32)
