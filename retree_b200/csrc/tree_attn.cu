@@ -169,13 +169,47 @@ __device__ __forceinline__ uint32_t stage_off(int r, int c) {
 // The split merge inside the cluster (every thread of every CTA calls it; the
 // cluster is the S = num_splits CTAs of one (kv head, tile), rank = split).
 // Each CTA has staged its unnormalised O rows and (m, l) in its own shared
-// memory.  Rank c merges the tile rows r = c, c + S, ...: first one thread per
-// row reads every rank's (m, l) and keeps the rank weights 2^(m_s - M) / L
-// (L = sum_s 2^(m_s - M) l_s, in rank order) in shared memory; then one thread
-// per (row, 4-dim chunk) reads every rank's chunk -- all loads in flight at
-// once -- and sums them in rank order (a rank of weight 0 is skipped, never
-// multiplied) into the bf16 output.  The last barrier keeps every CTA's
+// memory.  Rank c merges the tile rows r = c, c + S, ...: the rank weights of
+// a row are 2^(m_s - M) / L (L = sum_s 2^(m_s - M) l_s, in rank order), and the
+// chunks are summed in rank order (a rank of weight 0 -- no key of the row, or
+// a row it did not stage -- is skipped, never multiplied) into the bf16
+// output.  When every thread has at most one (row, 4-dim chunk) item, each
+// item's thread loads every rank's (m, l) and chunk at once and forms the
+// weights itself: one distributed-shared-memory round trip.  Otherwise one
+// thread per row forms the weights into a shared table first and the item
+// threads then load only the chunks.  The last barrier keeps every CTA's
 // shared memory until all ranks have read it.
+__device__ __forceinline__ float4 merge_chunk(const float4 (&o)[kMaxMerge], int S, const float* wrow) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int u = 0; u < kMaxMerge; ++u) {
+    const float wu = wrow[u];
+    if (u < S && wu != 0.f) {
+      acc.x = fmaf(wu, o[u].x, acc.x);
+      acc.y = fmaf(wu, o[u].y, acc.y);
+      acc.z = fmaf(wu, o[u].z, acc.z);
+      acc.w = fmaf(wu, o[u].w, acc.w);
+    }
+  }
+  return acc;
+}
+
+// The rank weights of one row from every rank's (m, l).
+__device__ __forceinline__ void merge_weights(const float2 (&ml)[kMaxMerge], float (&w)[kMaxMerge]) {
+  float M = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < kMaxMerge; ++u) M = fmaxf(M, ml[u].x);
+  float lsum = 0.f;
+#pragma unroll
+  for (int u = 0; u < kMaxMerge; ++u) {
+    w[u] = (M == -INFINITY || ml[u].x == -INFINITY) ? 0.f : ex2(ml[u].x - M);
+    lsum = fmaf(w[u], ml[u].y, lsum);
+  }
+  const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+#pragma unroll
+  for (int u = 0; u < kMaxMerge; ++u) w[u] = w[u] * inv;
+}
+
 __device__ __forceinline__ void merge_splits(const AttnParams& p, unsigned char* smem, int rank, int kvh, int row0,
                                              int rows_total) {
   __syncwarp();
@@ -186,55 +220,60 @@ __device__ __forceinline__ void merge_splits(const AttnParams& p, unsigned char*
   const int owned = rows_here > rank ? (rows_here - rank + S - 1) / S : 0;
   const uint32_t base = smem_u32(smem);
   float* wtab = reinterpret_cast<float*>(smem + kOffWeights);
-  for (int i = tid; i < owned; i += kAttnThreads) {
-    const int rr = rank + S * i;
-    float2 ml[kMaxMerge];
-#pragma unroll
-    for (int u = 0; u < kMaxMerge; ++u)
-      ml[u] = u < S ? ld_cluster_f32x2(cluster_map(base + kOffMl + rr * 8, u)) : make_float2(-INFINITY, 0.f);
-    float M = -INFINITY;
-#pragma unroll
-    for (int u = 0; u < kMaxMerge; ++u) M = fmaxf(M, ml[u].x);
-    float w[kMaxMerge];
-    float lsum = 0.f;
-#pragma unroll
-    for (int u = 0; u < kMaxMerge; ++u) {
-      w[u] = (M == -INFINITY || ml[u].x == -INFINITY) ? 0.f : ex2(ml[u].x - M);
-      lsum = fmaf(w[u], ml[u].y, lsum);
-    }
-    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-#pragma unroll
-    for (int u = 0; u < kMaxMerge; ++u) wtab[i * kMaxMerge + u] = w[u] * inv;
-  }
-  __syncthreads();
-  for (int it = tid; it < owned * 32; it += kAttnThreads) {
-    const int i = it >> 5, c = it & 31;
-    const int rr = rank + S * i;
-    const uint32_t off = base + stage_off(rr, c);
-    float wu[kMaxMerge];
-    float4 o[kMaxMerge];
-#pragma unroll
-    for (int u = 0; u < kMaxMerge; ++u) {
-      wu[u] = wtab[i * kMaxMerge + u];
-      o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (u < S && wu[u] != 0.f) o[u] = ld_cluster_f32x4(cluster_map(off, u));
-    }
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int u = 0; u < kMaxMerge; ++u) {
-      if (u < S && wu[u] != 0.f) {
-        acc.x = fmaf(wu[u], o[u].x, acc.x);
-        acc.y = fmaf(wu[u], o[u].y, acc.y);
-        acc.z = fmaf(wu[u], o[u].z, acc.z);
-        acc.w = fmaf(wu[u], o[u].w, acc.w);
-      }
-    }
+  auto store = [&](int rr, int c, const float4& acc) {
     const int R = row0 + rr;
     const int node = R / G, h = kvh * G + (R - node * G);
     uint2 pk;
     pk.x = pack_bf16x2(acc.x, acc.y);
     pk.y = pack_bf16x2(acc.z, acc.w);
     *reinterpret_cast<uint2*>(p.out + node * p.out_tok_stride + h * p.out_head_stride + c * 8) = pk;
+  };
+  if (owned * 32 <= kAttnThreads) {  // the same in every thread of the CTA
+    const int it = tid;
+    if (it < owned * 32) {
+      const int i = it >> 5, c = it & 31;
+      const int rr = rank + S * i;
+      const uint32_t off = base + stage_off(rr, c);
+      float2 ml[kMaxMerge];
+      float4 o[kMaxMerge];
+#pragma unroll
+      for (int u = 0; u < kMaxMerge; ++u) {
+        ml[u] = make_float2(-INFINITY, 0.f);
+        o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (u < S) {
+          ml[u] = ld_cluster_f32x2(cluster_map(base + kOffMl + rr * 8, u));
+          o[u] = ld_cluster_f32x4(cluster_map(off, u));
+        }
+      }
+      float w[kMaxMerge];
+      merge_weights(ml, w);
+      store(rr, c, merge_chunk(o, S, w));
+    }
+  } else {
+    for (int i = tid; i < owned; i += kAttnThreads) {
+      const int rr = rank + S * i;
+      float2 ml[kMaxMerge];
+#pragma unroll
+      for (int u = 0; u < kMaxMerge; ++u)
+        ml[u] = u < S ? ld_cluster_f32x2(cluster_map(base + kOffMl + rr * 8, u)) : make_float2(-INFINITY, 0.f);
+      float w[kMaxMerge];
+      merge_weights(ml, w);
+#pragma unroll
+      for (int u = 0; u < kMaxMerge; ++u) wtab[i * kMaxMerge + u] = w[u];
+    }
+    __syncthreads();
+    for (int it = tid; it < owned * 32; it += kAttnThreads) {
+      const int i = it >> 5, c = it & 31;
+      const int rr = rank + S * i;
+      const uint32_t off = base + stage_off(rr, c);
+      float4 o[kMaxMerge];
+#pragma unroll
+      for (int u = 0; u < kMaxMerge; ++u) {
+        o[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (u < S && wtab[i * kMaxMerge + u] != 0.f) o[u] = ld_cluster_f32x4(cluster_map(off, u));
+      }
+      store(rr, c, merge_chunk(o, S, wtab + i * kMaxMerge));
+    }
   }
   __syncwarp();
   cluster_sync_all();
