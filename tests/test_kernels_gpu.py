@@ -123,6 +123,23 @@ def test_topk_fp16_matches_oracle(k):
     _check_topk(xh, k, dev, torch.float16)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_topk_rows_with_more_nans_than_k(dtype):
+    # NaN ranks first (ties by index): rows with fewer NaNs than k, more NaNs than k
+    # spread over the chunks, and more than k inside one chunk (its k-th key is a NaN)
+    dev = cuda()
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((3, 151936)).astype(np.float32)
+    x[0, rng.choice(151936, 5, replace=False)] = np.nan
+    x[1, rng.choice(151936, 40, replace=False)] = np.nan
+    x[2, 100:140] = np.nan
+    if dtype == torch.bfloat16:
+        x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    for k in (16, 64):
+        ids, lz = _check_topk(x, k, dev, dtype)
+        assert np.all(np.isnan(lz))
+
+
 def test_topk_small_vocab_and_specials():
     dev = cuda()
     x = np.random.default_rng(3).standard_normal((4, 300)).astype(np.float32)
