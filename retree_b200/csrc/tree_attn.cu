@@ -6,25 +6,29 @@
 // Grid (split, kv_head, m_tile).  A CTA owns 128 query rows of one kv head --
 // row r of the tile is (node (t*128+r)/group, q head kv_head*group + (..)%group),
 // so the GQA group shares every K/V tile without repeat_kv -- and a contiguous
-// range of 128-key blocks.  Six warps:
-//   warp 4  TMA producer: K and V blocks (two 64-column SW128 boxes each) into a
-//           2-stage ring, no multicast;
-//   warp 5  MMA issuer (one lane): S_j = Q K_j^T into a double-buffered TMEM
-//           tile, then O += P_{j-1} V_{j-1}; owns the TMEM allocation;
-//   warps 0-3 softmax: one query row per thread (TMEM lane), read S_j with
-//           tcgen05.ld, apply scale and the mask, online softmax in the exp2
-//           domain with a lazy (>8 in log2) rescale of O done in TMEM, write
-//           P_j as bf16 into a SW128 K-major tile for the PV MMA, and write the
-//           tile's result (normalised bf16, or fp32 partial + (m, l) when the
-//           key range is split).
+// range of 128-key blocks.  Ten warps:
+//   warp 8  TMA producer: Q, then K (lane 0) and V (lane 1) blocks -- two
+//           64-column SW128 boxes each -- into 2-stage rings, no multicast;
+//   warp 9  MMA issuer (one lane): S_j = Q K_j^T into a double-buffered TMEM
+//           tile, then O += P_{j-1} V_{j-1} with P read from TMEM; owns the
+//           TMEM allocation (S0 | S1 | O | P0 P1, 512 columns);
+//   warps 0-7 softmax, two threads per query row (TMEM lane; 64 key columns
+//           each, row max and sum exchanged through shared memory): scale and
+//           mask S_j, online softmax in the exp2 domain (scale-and-shift and
+//           row sums as paired fp32 operations) with a lazy (>8 in log2)
+//           rescale of O done in TMEM, P_j as bf16 pairs into TMEM, and the
+//           tile's result.
+// When the key range is split, the splits of one (kv head, tile) either form
+// a thread-block cluster and merge their partial O rows over distributed
+// shared memory at the end of the kernel, or write fp32 partials + (m, l) to
+// a workspace that attn_combine_kernel merges (two warps per output row up to
+// kFastSplits splits, all loads of a row in flight at once; one warp beyond).
 // Every mbarrier wait is bounded (common.cuh): on time-out the CTA records
 // RT_DEV_WAIT_TIMEOUT, drains what it issued, frees TMEM and exits.
 //
 // warp-level path (fewer rows): one warp per query row set, shuffle-reduced
 // dot products and online softmax; same partial format.
-//
-// Splits are merged by attn_combine_kernel (two warps per output row up to
-// kFastSplits splits, all loads of a row in flight at once; one warp beyond).
+
 #include <cuda.h>
 #include <cuda_fp16.h>
 
