@@ -8,9 +8,11 @@
 //   * swap AB: the MMA's M = 128 side is 128 weight rows (output features),
 //     its N side the m tokens (padded to 16; two MMAs when m > 256), K in
 //     64-element (128-byte, SW128) blocks.  Accumulators live in TMEM.
-//   * warp 0 issues TMA loads of the W tile and the X rows into a 4-8 stage
-//     ring, warp 1 issues tcgen05.mma (one thread) and owns TMEM, warps 2-5
-//     run the epilogue.  Small m fits two CTAs per SM.
+//   * warp 0 issues TMA loads of the W tile and the X rows into a ring of
+//     stages (one 64-column K block a stage, or four where K is split over a
+//     cluster: fewer, longer transfers per weight row), warp 1 issues
+//     tcgen05.mma (one thread) and owns TMEM, warps 2-5 run the epilogue.
+//     Small m fits two CTAs per SM.
 //   * split-K fills the machine when N / 128 is small: the CTAs of one tile
 //     form a thread-block cluster along the split dimension; each parks its
 //     fp32 partial tile in shared memory and every CTA sums, for the tokens it
